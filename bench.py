@@ -1,0 +1,387 @@
+#!/usr/bin/env python
+"""Benchmark of the distributed CSR x dense SpMM (the hot path of DistSpMM) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...      (one rank per GPU)
+
+Workload: R-MAT scale 20, edge factor 16,
+(a,b,c,d) = (.57,.19,.19,.05), symmetrised, deduplicated, no self-loops (31.4 M nnz),
+values U(0,1); dense B 1,048,576 x 128 fp32 U(-1,1); 1-D row partition over the ranks,
+T = 4 tiles per rank, HSDMA allocation (task_dist 2), adaptive fetch (comm_type 2).
+All inputs are seeded synthetic data generated here. The matrix is fixed as N grows
+(strong scaling, as the reference partitions one matrix).
+
+A step is one distributed SpMM C = A.B over the whole matrix: every rank fetches its
+needed remote B rows (copy-engine bulk copies / NVLink gather kernels) and runs its
+SpMM segments. Metric: GFLOPS = 2.nnz.dims / t, t = device time of a step (CUDA events
+on the launching stream, mean over K steps, max over ranks). L2 is flushed between steps
+(a 512 MiB write outside the timed events). `e2e` times the same step through the C ABI
+from pinned host memory: H2D of the rank's owned B tiles, the step, D2H of its C rows.
+
+`--impl reference` times the CPU CSR x dense loop of the oracle (the reference has no CPU
+implementation of the path: its SpMM is cuSPARSE) with all host threads, on rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import csv
+import datetime
+import io
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "SpMM GFLOPS (2*nnz*N/t)"
+UNIT = "GFLOPS"
+
+
+def parse_args(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--scale", type=int, default=20)
+    ap.add_argument("--dims", type=int, default=128)
+    ap.add_argument("--n-rolls", type=int, default=4)
+    ap.add_argument("--task-dist", type=int, default=2)
+    ap.add_argument("--comm-type", type=int, default=2)
+    ap.add_argument("--seed", type=int, default=1)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-flush", action="store_true")
+    ap.add_argument("--profile", action="store_true",
+                    help="short run for a profiler: warmup + steps only, no e2e / CPU baseline / clocks")
+    return ap.parse_args(argv)
+
+
+def env_rank():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)),
+            int(os.environ.get("WORLD_SIZE", 1)))
+
+
+def workload_name(a):
+    return f"rmat{a.scale}_n{a.dims}"
+
+
+def config_of(a, world, nnz, M):
+    return {"workload": workload_name(a),
+            "matrix": f"R-MAT scale {a.scale}, ef 16, (.57,.19,.19,.05), symmetrised, dedup, no self-loops",
+            "rows": M, "nnz": nnz, "dims": a.dims, "n_rolls": a.n_rolls, "task_dist": a.task_dist,
+            "comm_type": a.comm_type, "parallelism": f"row1d_p{world}", "seed": a.seed,
+            "l2": "flushed between steps (512 MiB write)" if not a.no_flush else "not flushed",
+            "b": "U(-1,1) fp32 row-major", "values": "U(0,1) fp32"}
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def profile_traffic(workload):
+    """DRAM bytes per launch of the SpMM kernel from the committed ncu summary, if any."""
+    path = os.path.join(ROOT, "profiles", f"spmm_items_{workload}.md")
+    try:
+        txt = open(path).read()
+    except OSError:
+        return None
+    m = re.search(r"dram_bytes_per_launch:\s*([0-9.eE+]+)", txt)
+    return float(m.group(1)) if m else None
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.p = None
+
+    def start(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                      stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return None
+        self.p.terminate()
+        try:
+            self.p.wait(5)
+        except subprocess.TimeoutExpired:
+            self.p.kill()
+        self.f.seek(0)
+        rows = [r for r in csv.reader(io.StringIO(self.f.read())) if len(r) >= 9]
+        os.unlink(self.f.name)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if "Active" in v and "Not" not in v})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def cpu_spmm_baseline(A, B, budget_s=10.0, max_reps=5):
+    """Time the oracle's fp32 OpenMP CSR x dense loop (all host threads) on the full matrix,
+    or on a strided row sample when one pass would exceed the budget."""
+    import numpy as np
+
+    import oracle
+    threads = oracle.max_threads()
+    C = np.empty((A.num_rows, B.shape[1]), np.float32)
+    t0 = time.perf_counter()
+    oracle.spmm_f32(A.indptr, A.indices, A.values, B, threads=threads, out=C)
+    first = time.perf_counter() - t0
+    sample = "full matrix"
+    ip, ix, vv, nnz = A.indptr, A.indices, A.values, A.nnz
+    if first > budget_s / 2:
+        k = int(first / (budget_s / 8)) + 1
+        rows = np.arange(0, A.num_rows, k)
+        lens = np.diff(A.indptr)[rows]
+        ip = np.concatenate([[0], np.cumsum(lens)]).astype(np.int64)
+        sel = np.concatenate([np.arange(A.indptr[r], A.indptr[r + 1]) for r in rows])
+        ix, vv, nnz = A.indices[sel], A.values[sel], int(ip[-1])
+        C = np.empty((rows.size, B.shape[1]), np.float32)
+        sample = f"every {k}-th row ({rows.size} rows, {nnz} nnz)"
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while len(times) < max_reps and (not times or time.perf_counter() < t_end):
+        t0 = time.perf_counter()
+        oracle.spmm_f32(ip, ix, vv, B, threads=threads, out=C)
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    return {"value": round(2.0 * nnz * B.shape[1] / t / 1e9, 3), "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{sample}, dims {B.shape[1]}, median of {len(times)} passes"}
+
+
+def run_reference(a, rank, world):
+    """CPU arm: the oracle's fp32 OpenMP loop on rank 0 (other ranks exit without work)."""
+    if rank != 0:
+        return 0
+    import distspmm_b200 as d
+    A = d.gen_rmat(a.scale, seed=a.seed)
+    B = d.dense_b(A.num_cols, a.dims, seed=a.seed + 1)
+    import numpy as np
+
+    import oracle
+    threads = oracle.max_threads()
+    C = np.empty((A.num_rows, a.dims), np.float32)
+    t0 = time.perf_counter()
+    oracle.spmm_f32(A.indptr, A.indices, A.values, B, threads=threads, out=C)
+    one = time.perf_counter() - t0
+    # bound the whole run to about two minutes
+    k = max(1, int(one * (a.steps + a.warmup) / 120.0) + 1)
+    ip, ix, vv, nnz, sample = A.indptr, A.indices, A.values, A.nnz, "full matrix"
+    if k > 1:
+        rows = np.arange(0, A.num_rows, k)
+        lens = np.diff(A.indptr)[rows]
+        ip = np.concatenate([[0], np.cumsum(lens)]).astype(np.int64)
+        sel = np.concatenate([np.arange(A.indptr[r], A.indptr[r + 1]) for r in rows])
+        ix, vv, nnz = A.indices[sel], A.values[sel], int(ip[-1])
+        C = np.empty((rows.size, a.dims), np.float32)
+        sample = f"every {k}-th row ({rows.size} rows, {nnz} nnz)"
+    for _ in range(a.warmup):
+        oracle.spmm_f32(ip, ix, vv, B, threads=threads, out=C)
+    t0 = time.perf_counter()
+    for _ in range(a.steps):
+        oracle.spmm_f32(ip, ix, vv, B, threads=threads, out=C)
+    dt = (time.perf_counter() - t0) / max(a.steps, 1)
+    v = 2.0 * nnz * a.dims / dt / 1e9
+    line = {"metric": METRIC, "value": round(v, 3), "unit": UNIT, "n_gpus": world, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+            "config": config_of(a, 1, A.nnz, A.num_rows),
+            "cpu_baseline": {"value": round(v, 3), "unit": UNIT, "cores": threads, "kind": "port",
+                             "sample": f"{sample}, dims {a.dims}"},
+            "e2e": {"value": round(v, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main(argv=None):
+    a = parse_args(argv)
+    rank, local_rank, world = env_rank()
+    if a.impl == "reference":
+        return run_reference(a, rank, world)
+    import numpy as np
+    import torch
+
+    import distspmm_b200 as d
+    from distspmm_b200 import planner
+    from distspmm_b200.dist import TorchComm, connect_peers, distributed_plan, global_plan, make_rank
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    comm = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+        comm = TorchComm()
+
+    # every rank builds the whole matrix (the reference: every rank reads the whole file)
+    A = d.gen_rmat(a.scale, seed=a.seed)
+    M, nnz = A.num_rows, A.nnz
+    lb, ub = planner.partition_bounds(M, world, rank)
+    local = planner.partition(A, lb, ub)
+    if comm is None:
+        tiling = planner.tile(local, a.n_rolls)
+        plan = global_plan([tiling], a.task_dist, a.n_rolls)
+    else:
+        tiling, plan = distributed_plan(comm, local, a.n_rolls, a.task_dist)
+    R = make_rank(local, rank, world, local_rank, a.dims, M, lb, tiling, plan, a.comm_type, "h100", 4)
+    if comm is not None:
+        connect_peers(comm, R)
+    st = R.stats()
+    s = torch.cuda.Stream(dev)
+    R.fill_b(a.seed + 1, s.cuda_stream)
+    torch.cuda.synchronize(dev)
+    if comm is not None:
+        comm.barrier()
+    flush = torch.empty(512 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+
+    def flush_l2():
+        if not a.no_flush:
+            with torch.cuda.stream(s):
+                flush.fill_(1.0)
+
+    # warm-up (untimed)
+    for _ in range(a.warmup):
+        R.step(s.cuda_stream)
+    torch.cuda.synchronize(dev)
+    if comm is not None:
+        comm.barrier()
+
+    clocks = Clocks(local_rank) if not a.profile else None
+    if clocks:
+        clocks.start()
+    step_ms, compute_ms = [], []
+    torch.cuda.synchronize(dev)
+    if comm is not None:
+        comm.barrier()
+    t_wall = time.perf_counter()
+    for _ in range(a.steps):
+        flush_l2()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        R.step(s.cuda_stream)
+        e1.record(s)
+        e1.synchronize()
+        step_ms.append(e0.elapsed_time(e1))
+        compute_ms.append(R.last_compute_ms())
+    torch.cuda.synchronize(dev)
+    if comm is not None:
+        comm.barrier()
+    wall = time.perf_counter() - t_wall
+    clk = clocks.stop() if clocks else None
+
+    mean_step = statistics.mean(step_ms)
+    mean_compute = statistics.mean(compute_ms)
+    if comm is not None:
+        t_step = comm.allreduce_max(mean_step)
+        t_comp_max = comm.allreduce_max(mean_compute)
+    else:
+        t_step, t_comp_max = mean_step, mean_compute
+    value = 2.0 * nnz * a.dims / (t_step * 1e-3) / 1e9
+
+    # algorithmic HBM bytes of this rank's SpMM (nnz*12 + U*N*4 + m*N*4)
+    alg_bytes = st["nnz_local"] * 12 + st["distinct_cols"] * a.dims * 4 + st["m_local"] * a.dims * 4
+    peak, peak_kind = measured_peaks()
+    achieved = alg_bytes / (mean_compute * 1e-3) / 1e9
+
+    # end to end through the C ABI: pinned host B (owned tiles uploaded), step, C to host
+    e2e = None
+    if not a.no_e2e and not a.profile:
+        Bh = torch.empty((M, a.dims), dtype=torch.float32, pin_memory=True)
+        d.dense_b(M, a.dims, a.seed + 1, out=Bh.numpy())
+        Ch = torch.empty((max(ub - lb, 1), a.dims), dtype=torch.float32, pin_memory=True)
+        e2e_ms = []
+        for it in range(a.warmup + a.steps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(s)
+            R.upload_b_ptr(Bh.data_ptr(), s.cuda_stream)
+            if comm is not None:  # peers read this rank's tiles only after every upload landed
+                s.synchronize()
+                comm.barrier()
+            R.step(s.cuda_stream)
+            if ub > lb:
+                R.download_c_ptr(Ch.data_ptr(), s.cuda_stream)
+            e1.record(s)
+            e1.synchronize()
+            if it >= a.warmup:
+                e2e_ms.append(e0.elapsed_time(e1))
+            if comm is not None:  # nobody overwrites its tiles while a peer may still read them
+                comm.barrier()
+        t_e2e = statistics.mean(e2e_ms)
+        if comm is not None:
+            t_e2e = comm.allreduce_max(t_e2e)
+        # spot check of the result against the oracle on a few rows of this rank
+        import oracle
+        rng = np.random.default_rng(rank)
+        rows = rng.choice(ub - lb, size=min(64, ub - lb), replace=False) if ub > lb else np.zeros(0, int)
+        lens = np.diff(local.indptr)[rows]
+        ip = np.concatenate([[0], np.cumsum(lens)]).astype(np.int64)
+        sel = np.concatenate([np.arange(local.indptr[r], local.indptr[r + 1]) for r in rows]) if rows.size else \
+            np.zeros(0, np.int64)
+        ref, ab = oracle.spmm_f64(ip, local.indices[sel], local.values[sel], Bh.numpy())
+        ok, worst = oracle.check_close(Ch.numpy()[rows], ref, ab, 1e-5)
+        if comm is not None:
+            worst = comm.allreduce_max(worst)
+            ok = worst <= 1.0
+        e2e = {"value": round(2.0 * nnz * a.dims / (t_e2e * 1e-3) / 1e9, 3), "unit": UNIT,
+               "ms_per_step": round(t_e2e, 4), "h2d_bytes_per_step": st["owned_rows"] * a.dims * 4,
+               "d2h_bytes_per_step": (ub - lb) * a.dims * 4,
+               "check": {"rows": int(rows.size), "worst_err_over_tol": round(worst, 4), "ok": bool(ok)}}
+
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline and not a.profile:
+        cpu = cpu_spmm_baseline(A, d.dense_b(M, a.dims, a.seed + 1))
+
+    fetch_bytes = st["fetch_bytes"]
+    if comm is not None:
+        fetch_bytes = comm.allreduce_sum_i64(fetch_bytes)
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": a.steps,
+        "warmup": a.warmup, "ms_per_step": round(t_step, 4), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config_of(a, world, nnz, M),
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": profile_traffic(workload_name(a)),
+                     "kernel": "spmm_items_kernel (+fixup)", "rank": rank,
+                     "alg_bytes_per_launch": alg_bytes, "launch_ms": round(mean_compute, 4),
+                     "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})"},
+        "e2e": e2e, "cpu_baseline": cpu, "clocks": clk,
+        "gpu_launches": a.steps * st["kernels_per_step"],
+        "nvlink": {"fetched_bytes_per_step": fetch_bytes,
+                   "max_rank_compute_ms": round(t_comp_max, 4)},
+        "wall_s_timed_region": round(wall, 3),
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    R.close()
+    if comm is not None:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

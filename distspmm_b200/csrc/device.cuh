@@ -1,0 +1,68 @@
+// device.cuh — device-side declarations shared by the CUDA translation units.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "common.h"
+
+namespace dsp {
+
+constexpr int kSpmmThreads = 256;
+
+// Arguments of one SpMM launch (passed by value to the kernels).
+struct SpmmArgs {
+  const int64_t *item_ptr;  // [n_items + 1]
+  const int32_t *item_out;  // [n_items]  row (>= 0) or -(slot + 1)
+  int64_t n_items;
+  const int32_t *split_row;  // [n_split]
+  const int32_t *split_ptr;  // [n_split + 1] slot ranges
+  int64_t n_split;
+  const int32_t *cols;  // [nnz]
+  const float *vals;    // [nnz]
+  const float *B;
+  int64_t ldb;
+  float *C;
+  int64_t ldc;
+  float *partial;  // [pieces][N]
+  int N;
+};
+
+struct SpmmShape {
+  int W;           // floats per vector (4 or 1)
+  int LPR;         // lanes per item
+  int VPL;         // vectors per lane
+  int chunk_cols;  // columns per blockIdx.y
+  int chunks;
+};
+
+SpmmShape spmm_shape(int N, const float *B, int64_t ldb, const float *C, int64_t ldc);
+int launch_spmm(const SpmmArgs &a, bool accumulate, cudaStream_t stream);
+int launch_fill_dense(float *B, int64_t row0, int64_t rows, int64_t ld, int64_t ncols, uint64_t seed,
+                      cudaStream_t stream);
+int launch_fill_const(float *B, int64_t n, float v, cudaStream_t stream);
+void prefer_l1_carveout();
+int dev_upload(void *dptr_out, const void *host, size_t bytes);
+
+// A CSR operand in device memory, cut into work items.
+struct DevOperand {
+  int device = 0;
+  int64_t rows = 0, cols = 0, nnz = 0;
+  int64_t n_items = 0, n_split = 0, pieces = 0, piece_cap = 0, max_row_len = 0;
+  int64_t *d_item_ptr = nullptr;
+  int32_t *d_item_out = nullptr;
+  int32_t *d_split_row = nullptr;
+  int32_t *d_split_ptr = nullptr;
+  int32_t *d_cols = nullptr;
+  float *d_vals = nullptr;
+
+  // Rows i < m with nonzeros [row_ptr[i], row_ptr[i+1]) of indices/values (offsets are
+  // absolute; first_nz is subtracted); row_ids[i] is the output row (nullptr = i).
+  int upload(int device, int64_t rows, int64_t cols, const int64_t *row_ptr, const int32_t *row_ids, int64_t m,
+             const int64_t *indices, const float *values, int64_t first_nz, int64_t nnz, int64_t piece_cap,
+             bool include_empty);
+  void release();
+  int64_t device_bytes() const;
+  SpmmArgs args(const float *B, int64_t ldb, float *C, int64_t ldc, int N, float *partial) const;
+};
+
+}  // namespace dsp

@@ -1,0 +1,514 @@
+// rank.cu — one GPU's share of the distributed SpMM.
+//
+// Data layout in HBM (per rank):
+//   B     [M x dims] fp32 row-major, full height. The tiles this rank owns live at their
+//         global row offsets; remote rows fetched for a step land at the same offsets, so
+//         the SpMM kernels use global column ids unchanged and no receive buffer is ever
+//         recycled (the reference's 4-slot ring of src/dist_spmm_node.cu:199-203 with its
+//         reuse race, replaced by one full-height buffer: 180 GB HBM holds B at every
+//         configuration this engine targets).
+//   C     [m_local x dims] fp32 row-major.
+//   A     one DevOperand per segment: segment k holds the local nonzeros whose column
+//         tile is owned by rank (me + k) % P (the reference's visit order,
+//         src/dist_spmm_node.cu:339-343). Segment 0 lists every local row (it writes C);
+//         later segments list only rows with nonzeros there (they accumulate).
+//   scratch: partial rows of heavy-row pieces, shared by the segments (they run in order
+//         on one stream).
+//
+// One step: the fetch streams (high priority) pull each peer's tiles — bulk tiles with one
+// copy-engine copy each (cudaMemcpyAsync over NVLink, as nvshmemx_getmem_on_stream in
+// src/comm_man.h:503), sparse tiles with one gather kernel per peer that moves the merged
+// needed rows with 128-bit loads from the peer's B (src/comm_man.h:72-101) — while the
+// compute stream runs segment 0, then waits for peer k's fetch event before segment k.
+#include <cuda_runtime.h>
+#include <string.h>
+
+#include "device.cuh"
+#include "internal.h"
+
+namespace dsp {
+
+namespace {
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+#define DSP_CUDA(call)                                                                      \
+  do {                                                                                      \
+    cudaError_t e_ = (call);                                                                \
+    if (e_ != cudaSuccess) return fail(DSP_ERR_CUDA, "%s: %s", #call, cudaGetErrorString(e_)); \
+  } while (0)
+
+__device__ __forceinline__ float4 ld_peer_v4(const float *p) {
+  float4 v;
+  asm volatile("ld.global.L1::no_allocate.v4.f32 {%0,%1,%2,%3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "l"(p));
+  return v;
+}
+
+// Sparsity-aware fetch: dst[r, :] = src[r, :] for every global row r in rows[0..n).
+// One warp per group of kRows rows; all loads of the group are issued before the stores.
+template <int kRows>
+__global__ void __launch_bounds__(256) gather_rows_v4_kernel(float *__restrict__ dst, const float *__restrict__ src,
+                                                             const int32_t *__restrict__ rows, int64_t n,
+                                                             int64_t ld, int nvec) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t g = warp * kRows; g < n; g += nwarps * kRows) {
+    int32_t r[kRows];
+#pragma unroll
+    for (int k = 0; k < kRows; ++k) r[k] = g + k < n ? __ldg(rows + g + k) : -1;
+    for (int v = lane; v < nvec; v += 32) {
+      float4 x[kRows];
+#pragma unroll
+      for (int k = 0; k < kRows; ++k)
+        if (r[k] >= 0) x[k] = ld_peer_v4(src + (int64_t)r[k] * ld + 4 * v);
+#pragma unroll
+      for (int k = 0; k < kRows; ++k)
+        if (r[k] >= 0) *reinterpret_cast<float4 *>(dst + (int64_t)r[k] * ld + 4 * v) = x[k];
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256) gather_rows_f1_kernel(float *__restrict__ dst, const float *__restrict__ src,
+                                                             const int32_t *__restrict__ rows, int64_t n,
+                                                             int64_t ld, int dims) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t g = warp; g < n; g += nwarps) {
+    const int64_t r = __ldg(rows + g);
+    for (int c = lane; c < dims; c += 32) dst[r * ld + c] = src[r * ld + c];
+  }
+}
+
+}  // namespace
+
+int launch_gather_rows(float *dst, const float *src, const int32_t *rows, int64_t n, int dims, cudaStream_t s) {
+  if (n <= 0) return DSP_OK;
+  const bool v4 = dims % 4 == 0 && ((uintptr_t)dst & 15) == 0 && ((uintptr_t)src & 15) == 0;
+  const int64_t warps_needed = (n + 3) / 4;
+  const int64_t blocks = std::min<int64_t>((warps_needed + 7) / 8, 148 * 8);
+  if (v4)
+    gather_rows_v4_kernel<4><<<(unsigned)blocks, 256, 0, s>>>(dst, src, rows, n, dims, dims / 4);
+  else
+    gather_rows_f1_kernel<<<(unsigned)blocks, 256, 0, s>>>(dst, src, rows, n, dims, dims);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? DSP_OK : fail(DSP_ERR_CUDA, "gather launch: %s", cudaGetErrorString(e));
+}
+
+}  // namespace dsp
+
+using namespace dsp;
+
+struct dsp_rank {
+  int me = 0, P = 1, device = 0, dims = 0, T = 0, n_streams = 1;
+  int64_t cpt = 0, M = 0, m_lb = 0, m_local = 0, nnz_local = 0;
+  std::vector<int32_t> remap;
+  std::vector<uint8_t> sparse;
+  float *B = nullptr, *C = nullptr, *scratch = nullptr;
+  int64_t scratch_floats = 0;
+
+  struct Segment {
+    int owner = 0;
+    DevOperand op;
+  };
+  std::vector<Segment> segs;  // segs[k].owner == (me + k) % P
+
+  struct Fetch {
+    std::vector<std::pair<int64_t, int64_t>> bulk;  // (first row, rows)
+    int32_t *d_rows = nullptr;                      // sparse gather rows (global ids)
+    int64_t n_rows = 0;
+  };
+  std::vector<Fetch> fetch;  // by segment index k (k = 0 unused)
+
+  std::vector<const float *> peer_B;
+  std::vector<int> peer_dev;
+  std::vector<bool> peer_ipc;
+  std::vector<int64_t> owned;  // owned tiles
+
+  cudaStream_t compute = nullptr;
+  std::vector<cudaStream_t> fstreams;
+  cudaEvent_t ev_start = nullptr, ev_c0 = nullptr, ev_c1 = nullptr;
+  std::vector<cudaEvent_t> ev_fetch;
+  dsp_rank_stats stats{};
+};
+
+namespace {
+
+int build_segments(dsp_rank *r, const dsp_csr *a) {
+  const int P = r->P, me = r->me;
+  const int64_t m = a->num_rows, cpt = r->cpt;
+  auto seg_of = [&](int64_t c) { return (r->remap[(size_t)(c / cpt)] - me + P) % P; };
+  r->segs.resize((size_t)P);
+  const int64_t piece_cap = default_piece_cap(r->dims);
+  for (int k = 0; k < P; ++k) {
+    auto &S = r->segs[(size_t)k];
+    S.owner = (me + k) % P;
+    std::vector<int64_t> cnt((size_t)m + 1, 0);
+    parallel_for(m, [&](int64_t b, int64_t e) {
+      for (int64_t i = b; i < e; ++i) {
+        int64_t n = 0;
+        for (int64_t j = a->indptr[i]; j < a->indptr[i + 1]; ++j) n += seg_of(a->indices[j]) == k;
+        cnt[(size_t)i] = n;
+      }
+    }, 1024);
+    std::vector<int32_t> rows;
+    std::vector<int64_t> ptr(1, 0);
+    for (int64_t i = 0; i < m; ++i) {
+      if (k > 0 && cnt[(size_t)i] == 0) continue;
+      rows.push_back((int32_t)i);
+      ptr.push_back(ptr.back() + cnt[(size_t)i]);
+    }
+    const int64_t nr = (int64_t)rows.size(), nz = ptr.back();
+    std::vector<int64_t> idx((size_t)std::max<int64_t>(nz, 1));
+    std::vector<float> val((size_t)std::max<int64_t>(nz, 1));
+    parallel_for(nr, [&](int64_t b, int64_t e) {
+      for (int64_t q = b; q < e; ++q) {
+        const int64_t i = rows[(size_t)q];
+        int64_t p = ptr[(size_t)q];
+        for (int64_t j = a->indptr[i]; j < a->indptr[i + 1]; ++j)
+          if (seg_of(a->indices[j]) == k) {
+            idx[(size_t)p] = a->indices[j];
+            val[(size_t)p] = a->values[j];
+            ++p;
+          }
+      }
+    }, 1024);
+    int rc = S.op.upload(r->device, m, r->M, ptr.data(), k == 0 ? nullptr : rows.data(), nr, idx.data(),
+                         val.data(), 0, nz, piece_cap, k == 0);
+    if (rc) return rc;
+    r->scratch_floats = std::max(r->scratch_floats, S.op.pieces * (int64_t)r->dims);
+  }
+  return DSP_OK;
+}
+
+int build_fetch(dsp_rank *r, const dsp_rank_desc *d) {
+  const int P = r->P, T = r->T;
+  std::vector<int64_t> nnz_t((size_t)T, 0);
+  for (int64_t j = 0; j < d->local->nnz; ++j) nnz_t[(size_t)(d->local->indices[j] / r->cpt)]++;
+  r->fetch.assign((size_t)P, dsp_rank::Fetch());
+  for (int k = 1; k < P; ++k) {
+    const int q = (r->me + k) % P;
+    auto &F = r->fetch[(size_t)k];
+    std::vector<int32_t> rows;
+    for (int t = 0; t < T; ++t) {  // tiles of q in ascending order (task_assignments[q])
+      if (r->remap[(size_t)t] != q || nnz_t[(size_t)t] == 0) continue;  // src/dist_spmm_node.cu:344
+      const int64_t row0 = (int64_t)t * r->cpt;
+      if (r->sparse[(size_t)t]) {
+        for (int64_t p = d->needed_offsets[t]; p < d->needed_offsets[t + 1]; ++p)
+          rows.push_back((int32_t)(row0 + d->needed_cols[p]));
+        r->stats.fetch_sparse_tiles++;
+      } else {
+        const int64_t n = std::min<int64_t>(r->cpt, r->M - row0);
+        if (n > 0) F.bulk.push_back({row0, n});
+        r->stats.fetch_bulk_tiles++;
+        r->stats.fetch_rows += n;
+      }
+    }
+    F.n_rows = (int64_t)rows.size();
+    r->stats.fetch_rows += F.n_rows;
+    if (F.n_rows) {
+      int rc = dev_upload(&F.d_rows, rows.data(), sizeof(int32_t) * rows.size());
+      if (rc) return rc;
+    }
+  }
+  r->stats.fetch_bytes = r->stats.fetch_rows * (int64_t)r->dims * 4;
+  return DSP_OK;
+}
+
+}  // namespace
+
+extern "C" int dsp_rank_create(const dsp_rank_desc *d, dsp_rank **out) {
+  DSP_TRY_ARG(d && out && d->local && d->remap, "dsp_rank_create: null argument");
+  DSP_TRY_ARG(d->world >= 1 && d->rank >= 0 && d->rank < d->world, "dsp_rank_create: rank %d of %d", d->rank,
+              d->world);
+  DSP_TRY_ARG(d->dims >= 1 && d->T >= 1 && d->cpt >= 1 && d->M >= 1, "dsp_rank_create: dims/T/cpt/M");
+  DSP_TRY_ARG(d->M <= INT32_MAX, "dsp_rank_create: M must fit int32");
+  DSP_TRY_ARG(d->local->num_cols == d->M, "dsp_rank_create: local matrix has %lld columns, M = %lld",
+              (long long)d->local->num_cols, (long long)d->M);
+  DSP_TRY_ARG(d->world == 1 || (d->sparse && d->needed_offsets), "dsp_rank_create: fetch plan missing");
+  *out = nullptr;
+  for (int t = 0; t < d->T; ++t)
+    DSP_TRY_ARG(d->remap[t] >= 0 && d->remap[t] < d->world, "dsp_rank_create: remap[%d] = %d", t, d->remap[t]);
+  DSP_TRY_ARG((int64_t)d->T * d->cpt >= d->M, "dsp_rank_create: T * cpt < M");
+  DeviceGuard g(d->device);
+  DSP_CUDA(cudaSetDevice(d->device));
+  prefer_l1_carveout();
+  dsp_rank *r = new dsp_rank();
+  r->me = d->rank;
+  r->P = d->world;
+  r->device = d->device;
+  r->dims = d->dims;
+  r->T = d->T;
+  r->n_streams = std::max(1, d->n_streams);
+  r->cpt = d->cpt;
+  r->M = d->M;
+  r->m_lb = d->m_lb;
+  r->m_local = d->local->num_rows;
+  r->nnz_local = d->local->nnz;
+  r->remap.assign(d->remap, d->remap + d->T);
+  if (d->sparse) r->sparse.assign(d->sparse, d->sparse + d->T);
+  else r->sparse.assign((size_t)d->T, 0);
+  r->peer_B.assign((size_t)r->P, nullptr);
+  r->peer_dev.assign((size_t)r->P, -1);
+  r->peer_ipc.assign((size_t)r->P, false);
+  for (int t = 0; t < d->T; ++t)
+    if (r->remap[(size_t)t] == r->me) r->owned.push_back(t);
+
+  auto bail = [&](int rc) {
+    dsp_rank_destroy(r);
+    return rc;
+  };
+  int rc;
+  cudaError_t e;
+  const size_t bbytes = sizeof(float) * (size_t)r->M * r->dims;
+  const size_t cbytes = sizeof(float) * (size_t)std::max<int64_t>(r->m_local, 1) * r->dims;
+  if ((e = cudaMalloc(&r->B, bbytes)) != cudaSuccess)
+    return bail(fail(DSP_ERR_NOMEM, "B (%zu bytes): %s", bbytes, cudaGetErrorString(e)));
+  if ((e = cudaMalloc(&r->C, cbytes)) != cudaSuccess)
+    return bail(fail(DSP_ERR_NOMEM, "C (%zu bytes): %s", cbytes, cudaGetErrorString(e)));
+  if ((rc = build_segments(r, d->local))) return bail(rc);
+  if (r->P > 1 && (rc = build_fetch(r, d))) return bail(rc);
+  if (r->scratch_floats > 0 && (e = cudaMalloc(&r->scratch, sizeof(float) * (size_t)r->scratch_floats)) != cudaSuccess)
+    return bail(fail(DSP_ERR_NOMEM, "scratch: %s", cudaGetErrorString(e)));
+  int lo = 0, hi = 0;
+  cudaDeviceGetStreamPriorityRange(&lo, &hi);
+  if ((e = cudaStreamCreateWithPriority(&r->compute, cudaStreamNonBlocking, lo)) != cudaSuccess)
+    return bail(fail(DSP_ERR_CUDA, "stream: %s", cudaGetErrorString(e)));
+  for (int i = 0; i < (r->P > 1 ? r->n_streams : 0); ++i) {
+    cudaStream_t s;
+    if ((e = cudaStreamCreateWithPriority(&s, cudaStreamNonBlocking, hi)) != cudaSuccess)
+      return bail(fail(DSP_ERR_CUDA, "stream: %s", cudaGetErrorString(e)));
+    r->fstreams.push_back(s);
+  }
+  if (cudaEventCreate(&r->ev_start) != cudaSuccess || cudaEventCreate(&r->ev_c0) != cudaSuccess ||
+      cudaEventCreate(&r->ev_c1) != cudaSuccess)
+    return bail(fail(DSP_ERR_CUDA, "event create failed"));
+  r->ev_fetch.assign((size_t)r->P, nullptr);
+  for (int k = 1; k < r->P; ++k)
+    if (cudaEventCreateWithFlags(&r->ev_fetch[(size_t)k], cudaEventDisableTiming) != cudaSuccess)
+      return bail(fail(DSP_ERR_CUDA, "event create failed"));
+
+  // statistics
+  auto &s = r->stats;
+  s.m_local = r->m_local;
+  s.nnz_local = r->nnz_local;
+  s.segments = 0;
+  s.launches_per_step = 0;
+  for (int k = 0; k < r->P; ++k) {
+    const auto &op = r->segs[(size_t)k].op;
+    if (k == 0 || op.n_items > 0) {
+      s.segments++;
+      s.kernels_per_step += (op.n_items > 0) + (op.n_split > 0);
+    }
+    if (k > 0) {
+      s.kernels_per_step += r->fetch[(size_t)k].n_rows > 0;
+      s.launches_per_step += (int64_t)r->fetch[(size_t)k].bulk.size();
+    }
+  }
+  s.launches_per_step += s.kernels_per_step;
+  for (int64_t t : r->owned) s.owned_rows += std::max<int64_t>(0, std::min<int64_t>(r->cpt, r->M - t * r->cpt));
+  {
+    std::vector<uint8_t> seen((size_t)r->M, 0);
+    for (int64_t j = 0; j < r->nnz_local; ++j) seen[(size_t)d->local->indices[j]] = 1;
+    for (auto x : seen) s.distinct_cols += x;
+  }
+  s.device_bytes = (int64_t)bbytes + (int64_t)cbytes + r->scratch_floats * 4;
+  for (auto &S : r->segs) s.device_bytes += S.op.device_bytes();
+  for (auto &F : r->fetch) s.device_bytes += F.n_rows * 4;
+  *out = r;
+  return DSP_OK;
+}
+
+extern "C" void dsp_rank_destroy(dsp_rank *r) {
+  if (!r) return;
+  DeviceGuard g(r->device);
+  if (r->compute) cudaStreamSynchronize(r->compute);
+  for (auto s : r->fstreams) cudaStreamSynchronize(s);
+  for (int p = 0; p < r->P; ++p)
+    if (r->peer_ipc[(size_t)p] && r->peer_B[(size_t)p]) cudaIpcCloseMemHandle((void *)r->peer_B[(size_t)p]);
+  for (auto &S : r->segs) S.op.release();
+  for (auto &F : r->fetch)
+    if (F.d_rows) cudaFree(F.d_rows);
+  if (r->B) cudaFree(r->B);
+  if (r->C) cudaFree(r->C);
+  if (r->scratch) cudaFree(r->scratch);
+  for (auto s : r->fstreams) cudaStreamDestroy(s);
+  if (r->compute) cudaStreamDestroy(r->compute);
+  for (auto ev : {r->ev_start, r->ev_c0, r->ev_c1})
+    if (ev) cudaEventDestroy(ev);
+  for (auto ev : r->ev_fetch)
+    if (ev) cudaEventDestroy(ev);
+  cudaGetLastError();
+  delete r;
+}
+
+extern "C" int dsp_rank_stats_get(const dsp_rank *r, dsp_rank_stats *s) {
+  DSP_TRY_ARG(r && s, "dsp_rank_stats_get: null argument");
+  *s = r->stats;
+  return DSP_OK;
+}
+
+extern "C" int dsp_rank_b_ptr(dsp_rank *r, float **B) {
+  DSP_TRY_ARG(r && B, "dsp_rank_b_ptr: null argument");
+  *B = r->B;
+  return DSP_OK;
+}
+
+extern "C" int dsp_rank_c_ptr(dsp_rank *r, float **C) {
+  DSP_TRY_ARG(r && C, "dsp_rank_c_ptr: null argument");
+  *C = r->C;
+  return DSP_OK;
+}
+
+extern "C" int dsp_rank_ipc_handle(dsp_rank *r, void *handle64) {
+  DSP_TRY_ARG(r && handle64, "dsp_rank_ipc_handle: null argument");
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+  DeviceGuard g(r->device);
+  cudaIpcMemHandle_t h;
+  DSP_CUDA(cudaIpcGetMemHandle(&h, r->B));
+  memcpy(handle64, &h, sizeof h);
+  return DSP_OK;
+}
+
+extern "C" int dsp_rank_open_peer(dsp_rank *r, int peer, const void *handle64) {
+  DSP_TRY_ARG(r && handle64 && peer >= 0 && peer < r->P && peer != r->me, "dsp_rank_open_peer: bad argument");
+  DeviceGuard g(r->device);
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle64, sizeof h);
+  void *p = nullptr;
+  DSP_CUDA(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+  r->peer_B[(size_t)peer] = (const float *)p;
+  r->peer_ipc[(size_t)peer] = true;
+  return DSP_OK;
+}
+
+extern "C" int dsp_rank_set_peer(dsp_rank *r, int peer, const float *peer_B, int peer_device) {
+  DSP_TRY_ARG(r && peer_B && peer >= 0 && peer < r->P && peer != r->me, "dsp_rank_set_peer: bad argument");
+  DeviceGuard g(r->device);
+  if (peer_device >= 0 && peer_device != r->device) {
+    int ok = 0;
+    DSP_CUDA(cudaDeviceCanAccessPeer(&ok, r->device, peer_device));
+    if (!ok) return fail(DSP_ERR_UNSUPPORTED, "device %d cannot access device %d", r->device, peer_device);
+    cudaError_t e = cudaDeviceEnablePeerAccess(peer_device, 0);
+    if (e == cudaErrorPeerAccessAlreadyEnabled) cudaGetLastError();
+    else if (e != cudaSuccess) return fail(DSP_ERR_CUDA, "enable peer access: %s", cudaGetErrorString(e));
+  }
+  r->peer_B[(size_t)peer] = peer_B;
+  r->peer_dev[(size_t)peer] = peer_device;
+  return DSP_OK;
+}
+
+extern "C" int dsp_rank_fill_b(dsp_rank *r, uint64_t seed, void *stream) {
+  DSP_TRY_ARG(r, "dsp_rank_fill_b: null rank");
+  DeviceGuard g(r->device);
+  for (int64_t t : r->owned) {
+    const int64_t row0 = t * r->cpt, n = std::min<int64_t>(r->cpt, r->M - row0);
+    if (n <= 0) continue;
+    int rc = launch_fill_dense(r->B + row0 * r->dims, row0, n, r->dims, r->dims, seed, (cudaStream_t)stream);
+    if (rc) return rc;
+  }
+  return DSP_OK;
+}
+
+extern "C" int dsp_rank_poison_remote(dsp_rank *r, void *stream) {
+  DSP_TRY_ARG(r, "dsp_rank_poison_remote: null rank");
+  DeviceGuard g(r->device);
+  std::vector<bool> own((size_t)r->T, false);
+  for (int64_t t : r->owned) own[(size_t)t] = true;
+  for (int t = 0; t < r->T; ++t) {
+    if (own[(size_t)t]) continue;
+    const int64_t row0 = (int64_t)t * r->cpt, n = std::min<int64_t>(r->cpt, r->M - row0);
+    if (n <= 0) continue;
+    int rc = launch_fill_const(r->B + row0 * r->dims, n * r->dims, nanf(""), (cudaStream_t)stream);
+    if (rc) return rc;
+  }
+  return DSP_OK;
+}
+
+extern "C" int dsp_rank_upload_b(dsp_rank *r, const float *B_host, void *stream) {
+  DSP_TRY_ARG(r && B_host, "dsp_rank_upload_b: null argument");
+  DeviceGuard g(r->device);
+  for (int64_t t : r->owned) {
+    const int64_t row0 = t * r->cpt, n = std::min<int64_t>(r->cpt, r->M - row0);
+    if (n <= 0) continue;
+    const size_t off = (size_t)row0 * r->dims;
+    DSP_CUDA(cudaMemcpyAsync(r->B + off, B_host + off, sizeof(float) * (size_t)n * r->dims, cudaMemcpyHostToDevice,
+                             (cudaStream_t)stream));
+  }
+  return DSP_OK;
+}
+
+extern "C" int dsp_rank_download_c(dsp_rank *r, float *C_host, void *stream) {
+  DSP_TRY_ARG(r && C_host, "dsp_rank_download_c: null argument");
+  DeviceGuard g(r->device);
+  if (r->m_local == 0) return DSP_OK;
+  DSP_CUDA(cudaMemcpyAsync(C_host, r->C, sizeof(float) * (size_t)r->m_local * r->dims, cudaMemcpyDeviceToHost,
+                           (cudaStream_t)stream));
+  return DSP_OK;
+}
+
+extern "C" int dsp_rank_step(dsp_rank *r, void *stream_v) {
+  DSP_TRY_ARG(r, "dsp_rank_step: null rank");
+  DeviceGuard g(r->device);
+  cudaStream_t stream = (cudaStream_t)stream_v;
+  for (int k = 1; k < r->P; ++k) {
+    const auto &F = r->fetch[(size_t)k];
+    if ((F.n_rows || !F.bulk.empty()) && !r->peer_B[(size_t)r->segs[(size_t)k].owner])
+      return fail(DSP_ERR_STATE, "rank %d: B of peer %d not attached", r->me, r->segs[(size_t)k].owner);
+  }
+  DSP_CUDA(cudaEventRecord(r->ev_start, stream));
+  DSP_CUDA(cudaStreamWaitEvent(r->compute, r->ev_start, 0));
+  for (auto s : r->fstreams) DSP_CUDA(cudaStreamWaitEvent(s, r->ev_start, 0));
+  // fetch: peers in ring order, spread over the fetch streams
+  std::vector<bool> has_fetch((size_t)r->P, false);
+  for (int k = 1; k < r->P; ++k) {
+    const auto &F = r->fetch[(size_t)k];
+    if (!F.n_rows && F.bulk.empty()) continue;
+    cudaStream_t fs = r->fstreams[(size_t)((k - 1) % r->n_streams)];
+    const float *src = r->peer_B[(size_t)r->segs[(size_t)k].owner];
+    for (const auto &b : F.bulk) {
+      const size_t off = (size_t)b.first * r->dims;
+      DSP_CUDA(cudaMemcpyAsync(r->B + off, src + off, sizeof(float) * (size_t)b.second * r->dims, cudaMemcpyDefault,
+                               fs));
+    }
+    int rc = launch_gather_rows(r->B, src, F.d_rows, F.n_rows, r->dims, fs);
+    if (rc) return rc;
+    DSP_CUDA(cudaEventRecord(r->ev_fetch[(size_t)k], fs));
+    has_fetch[(size_t)k] = true;
+  }
+  // compute: own segment writes C, every later segment accumulates after its fetch
+  DSP_CUDA(cudaEventRecord(r->ev_c0, r->compute));
+  for (int k = 0; k < r->P; ++k) {
+    const auto &op = r->segs[(size_t)k].op;
+    if (k > 0 && op.n_items == 0) continue;
+    if (has_fetch[(size_t)k]) DSP_CUDA(cudaStreamWaitEvent(r->compute, r->ev_fetch[(size_t)k], 0));
+    int rc = launch_spmm(op.args(r->B, r->dims, r->C, r->dims, r->dims, r->scratch), k > 0, r->compute);
+    if (rc) return rc;
+  }
+  DSP_CUDA(cudaEventRecord(r->ev_c1, r->compute));
+  for (int k = 1; k < r->P; ++k)
+    if (has_fetch[(size_t)k]) DSP_CUDA(cudaStreamWaitEvent(stream, r->ev_fetch[(size_t)k], 0));
+  DSP_CUDA(cudaStreamWaitEvent(stream, r->ev_c1, 0));
+  return DSP_OK;
+}
+
+extern "C" int dsp_rank_last_compute_ms(dsp_rank *r, float *ms) {
+  DSP_TRY_ARG(r && ms, "dsp_rank_last_compute_ms: null argument");
+  DeviceGuard g(r->device);
+  DSP_CUDA(cudaEventElapsedTime(ms, r->ev_c0, r->ev_c1));
+  return DSP_OK;
+}

@@ -1,0 +1,167 @@
+"""Multi-rank pipeline parity on the GPU(s) available: P ranks in one process (sharing a
+GPU when there is only one), each fetching remote B rows from its peers' buffers and
+accumulating segment by segment; the gathered C must match the oracle. Remote rows are
+poisoned with NaN before the step, so a row that was not fetched (or fetched after its
+use) makes C non-finite instead of passing silently."""
+import os
+import subprocess
+
+import numpy as np
+import pytest
+
+import distspmm_b200 as d
+import oracle
+from distspmm_b200 import planner
+
+pytestmark = pytest.mark.gpu
+RTOL = 1e-5
+
+
+def _devices(world):
+    import torch
+    n = torch.cuda.device_count()
+    return [p % n for p in range(world)]
+
+
+def _run_group(A, world, dims, rolls, task_dist, comm_type, seed=21, poison=True):
+    import torch
+    from distspmm_b200.dist import build_local_group
+    g = build_local_group(A, world, _devices(world), dims, rolls, task_dist, comm_type)
+    for r in g.ranks:
+        if poison:
+            r.poison_remote()
+        r.fill_b(seed)
+    for dev in set(_devices(world)):
+        torch.cuda.synchronize(dev)
+    g.step()
+    for dev in set(_devices(world)):
+        torch.cuda.synchronize(dev)
+    C = np.zeros((A.num_rows, dims), np.float32)
+    for r, (lb, ub) in zip(g.ranks, g.bounds):
+        if ub > lb:
+            part = np.empty((ub - lb, dims), np.float32)
+            r.download_c(part)
+            torch.cuda.synchronize(r.device)
+            C[lb:ub] = part
+    return g, C
+
+
+def _check(A, C, dims, seed=21):
+    B = d.dense_b(A.num_cols, dims, seed)
+    ref, ab = oracle.spmm_f64(A.indptr, A.indices, A.values, B)
+    assert np.isfinite(C).all(), "a remote row was used before it was fetched"
+    ok, worst = oracle.check_close(C, ref, ab, RTOL)
+    assert ok, worst
+
+
+@pytest.fixture(scope="module")
+def rmat12():
+    return d.gen_rmat(12, seed=8)
+
+
+@pytest.mark.parametrize("world,rolls,task_dist,comm_type", [
+    (2, 4, 2, 2), (2, 1, 0, 0), (2, 2, 0, 1), (4, 4, 2, 2), (4, 2, 1, 0), (8, 4, 2, 2), (8, 4, 0, 1),
+    (3, 3, 2, 2),
+])
+def test_group_parity_rmat(gpu, rmat12, world, rolls, task_dist, comm_type):
+    g, C = _run_group(rmat12, world, 128, rolls, task_dist, comm_type)
+    _check(rmat12, C, 128)
+    st = [r.stats() for r in g.ranks]
+    if comm_type == 0:
+        assert all(s["fetch_sparse_tiles"] == 0 for s in st)
+    if comm_type == 1:
+        assert all(s["fetch_bulk_tiles"] == 0 for s in st)
+    # fetched rows: sparse tiles move the merged needed lists, bulk tiles whole slices
+    for p, (r, s) in enumerate(zip(g.ranks, st)):
+        exp = 0
+        for t in range(g.plan.T):
+            if g.plan.remap[t] == p or g.tilings[p].nnz[t] == 0:
+                continue
+            exp += g.plan.n_col[t] if r.sparse[t] else g.tilings[p].n_slice[t]
+        assert s["fetch_rows"] == exp
+    g.close()
+
+
+@pytest.mark.parametrize("dims", [32, 100, 256])
+def test_group_parity_widths(gpu, rmat12, dims):
+    g, C = _run_group(rmat12, 4, dims, 2, 2, 2)
+    _check(rmat12, C, dims)
+    g.close()
+
+
+def test_group_stencil_and_uniform(gpu):
+    for A in (d.gen_stencil27(14, seed=2), d.gen_uniform(4096, 16, seed=3)):
+        g, C = _run_group(A, 4, 64, 4, 2, 2)
+        _check(A, C, 64)
+        g.close()
+
+
+def test_group_upload_from_host_and_repeat(gpu, rmat12):
+    """The e2e path: owned tiles uploaded from a host B, several steps in a row."""
+    import torch
+    from distspmm_b200.dist import build_local_group
+    dims = 64
+    g = build_local_group(rmat12, 2, _devices(2), dims, 4, 2, 2)
+    Bh = d.dense_b(rmat12.num_cols, dims, seed=99)
+    for it in range(3):
+        for r in g.ranks:
+            r.upload_b(Bh)
+        for dev in set(_devices(2)):
+            torch.cuda.synchronize(dev)
+        g.step()
+    C = np.zeros((rmat12.num_rows, dims), np.float32)
+    for r, (lb, ub) in zip(g.ranks, g.bounds):
+        part = np.empty((ub - lb, dims), np.float32)
+        r.download_c(part)
+        torch.cuda.synchronize(r.device)
+        C[lb:ub] = part
+    _check(rmat12, C, dims, seed=99)
+    g.close()
+
+
+def test_dsp_run_pipeline(gpu, rmat12):
+    """dsp_run: the whole dist_spmm_node program in-process, C returned to the host."""
+    import ctypes
+    from distspmm_b200 import _lib
+    world, dims = 4, 128
+    devs = (ctypes.c_int * world)(*_devices(world))
+    C = np.zeros((rmat12.num_rows, dims), np.float32)
+    c = rmat12.to_c()
+    a = _lib.dsp_args()
+    a.matrix = ctypes.pointer(c)
+    a.dims, a.task_dist, a.comm_type, a.n_rolls, a.repeat, a.n_streams = dims, 2, 2, 4, 7, 4
+    a.world, a.devices, a.platform, a.b_seed, a.b_ones = world, devs, 0, 21, 0
+    a.c_out = C.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+    rep = _lib.dsp_report()
+    _lib.call("dsp_run", ctypes.byref(a), ctypes.byref(rep))
+    _check(rmat12, C, dims)
+    assert rep.reps_counted == 2 and rep.avg_ms > 0 and rep.gflops > 0
+    # traffic = the reference formula summed over ranks
+    g_plan_traffic = 0
+    from distspmm_b200.dist import build_local_group
+    g = build_local_group(rmat12, world, _devices(world), dims, 4, 2, 2)
+    assert rep.traffic_intra == g.traffic_intra
+    assert list(rep.remap[:rep.T]) == g.plan.remap.tolist()
+    g.close()
+
+
+def test_cli_report_format(gpu, tmp_path):
+    from distspmm_b200 import build
+    A = d.gen_rmat(11, seed=1)
+    prefix = str(tmp_path / "g")
+    d.save_csr(prefix, A)
+    exe = os.path.join(build.BIN, "dist_spmm_node")
+    out = subprocess.run([exe, "-np", "2", prefix, "64", "2", "2", "2", "7", "4"], capture_output=True, text=True,
+                         timeout=300)
+    assert out.returncode == 0, out.stderr
+    lines = out.stdout.strip().splitlines()
+    assert lines[0] == "task_distribution: 2 and rolls:2"
+    assert len(lines[1].split()) == 4
+    assert lines[2] == f"Running dist_spmm_programs on {prefix} with [64] dims".replace("_programs", " programs")
+    keys = ["Processing time: (ms)", "Re-allocation time(all):", "Max memory used:", "Average time used:",
+            "Communication Traffic Intra :", "Communication Traffic Inter :", "Throughput:"]
+    for k, ln in zip(keys, lines[3:]):
+        assert ln.startswith(k), (k, ln)
+    # usage error and .mtx refusal as in the reference
+    assert subprocess.run([exe, prefix], capture_output=True).returncode != 0
+    assert subprocess.run([exe, "x.mtx", "64", "2", "2", "2", "7"], capture_output=True).returncode != 0

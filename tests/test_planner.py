@@ -1,0 +1,135 @@
+"""The native planner is bit-exact with the oracle (and through it, with the reference's
+golden vectors): tiling, needed sets, HSDMA, node merge, selector, traffic."""
+import json
+import os
+
+import numpy as np
+import pytest
+
+import distspmm_b200 as d
+import oracle
+from distspmm_b200 import planner
+from conftest import GOLDEN
+
+
+@pytest.fixture(scope="module")
+def rmat():
+    return d.gen_rmat(13, seed=11)
+
+
+def test_hsdma_matches_reference_golden():
+    for c in json.load(open(os.path.join(GOLDEN, "hsdma_cases.json"))):
+        got = planner.hsdma(np.array(c["demand"]), np.array(c["node_of_gpu"]), c["tasks_per_gpu"], c["max_inter"],
+                            c["max_intra"])
+        assert got.tolist() == c["remap"]
+
+
+def test_hsdma_random_matches_oracle():
+    rng = np.random.default_rng(1)
+    for _ in range(200):
+        P = int(rng.choice([1, 2, 4, 8]))
+        rolls = int(rng.integers(1, 6))
+        nodes = int(rng.choice([n for n in (1, 2, 4) if P % n == 0]))
+        D = rng.integers(0, int(rng.choice([2, 100, 100000])), size=(P, P * rolls))
+        node = np.repeat(np.arange(nodes), P // nodes)
+        assert (planner.hsdma(D, node, rolls) == oracle.hsdma(D, node, rolls)).all()
+
+
+@pytest.mark.parametrize("P,rolls", [(1, 1), (1, 4), (2, 4), (3, 2), (8, 4), (8, 1)])
+def test_tiling_matches_oracle(rmat, P, rolls):
+    T = P * rolls
+    for r in range(P):
+        lb, ub = planner.partition_bounds(rmat.num_rows, P, r)
+        loc = planner.partition(rmat, lb, ub)
+        a = planner.tile(loc, T)
+        b = oracle.tile(loc.indptr, loc.indices, rmat.num_cols, T)
+        assert a.cpt == b["cpt"]
+        for k in ("n_col", "n_slice", "nnz", "offsets", "needed"):
+            assert np.array_equal(getattr(a, k), b[k]), k
+
+
+def test_tiling_odd_sizes():
+    # columns not divisible by T, T > columns, empty local matrix
+    A = d.gen_uniform(37, 5, seed=2)
+    for T in (1, 4, 7, 36, 37, 50):
+        a = planner.tile(A, T)
+        b = oracle.tile(A.indptr, A.indices, A.num_cols, T)
+        assert a.cpt == b["cpt"] and np.array_equal(a.n_col, b["n_col"]) and np.array_equal(a.needed, b["needed"])
+        assert np.array_equal(a.n_slice, b["n_slice"])
+    E = planner.partition(A, 5, 5)
+    a = planner.tile(E, 4)
+    assert a.n_col.tolist() == [0] * 4 and a.n_slice.tolist() == [0] * 4
+
+
+def test_merge_matches_oracle(rmat):
+    P, rolls = 4, 3
+    T = P * rolls
+    tl = []
+    for r in range(P):
+        lb, ub = planner.partition_bounds(rmat.num_rows, P, r)
+        tl.append(planner.tile(planner.partition(rmat, lb, ub), T))
+    counts = np.stack([t.n_col for t in tl])
+    cols = np.concatenate([t.needed for t in tl])
+    n1, off1, m1 = planner.merge_needed(counts, cols)
+    n2, off2, m2 = oracle.merge(counts, cols, tl[0].cpt)
+    assert np.array_equal(n1, n2) and np.array_equal(off1, off2) and np.array_equal(m1, m2)
+    # on one node the union over all ranks is the set of nonempty columns of the whole matrix
+    whole = planner.tile(rmat, T)
+    assert np.array_equal(n1, whole.n_col) and np.array_equal(m1, whole.needed)
+
+
+def test_selector_matches_oracle_and_golden():
+    rng = np.random.default_rng(3)
+    T = 64
+    for platform, model in (("h100", oracle.H100_INTRA), ("a800", oracle.A800_INTRA)):
+        for dims in (1, 4, 16, 32, 64, 100, 128, 256, 512):
+            n_slice = rng.integers(0, 5000, T).astype(np.int32)
+            n_col = (rng.random(T) * (n_slice + 1)).astype(np.int32)
+            for ct in (0, 1, 2):
+                a = planner.comm_select(ct, dims, n_col, n_slice, platform)
+                b = oracle.select(ct, dims, model, n_col, n_slice)
+                assert np.array_equal(a, b), (platform, dims, ct)
+    # inter-tier decisions too
+    si, se = planner.comm_select(2, 128, np.array([1, 50]), np.array([100, 60]), "h100", with_inter=True)
+    assert se.tolist() == oracle.select(2, 128, oracle.H100_INTER, np.array([1, 50]), np.array([100, 60])).tolist()
+
+
+def test_model_presets_are_reference_constants():
+    m = planner.comm_model_preset("h100", 0)
+    assert (m.a, m.b, m.c, m.u) == tuple(float(np.float32(x)) for x in oracle.H100_INTRA)
+    m = planner.comm_model_preset("a800", 1)
+    assert (m.a, m.b, m.c, m.u) == tuple(float(np.float32(x)) for x in oracle.A800_INTER)
+
+
+def test_traffic_matches_oracle():
+    rng = np.random.default_rng(4)
+    for _ in range(50):
+        T = 32
+        remap = rng.integers(0, 8, T)
+        sp = rng.integers(0, 2, T)
+        n_col = rng.integers(0, 10000, T)
+        n_slice = rng.integers(0, 10000, T)
+        for me in range(8):
+            assert planner.traffic_intra(me, remap, sp, n_col, n_slice, 128) == \
+                oracle.traffic_intra(me, remap, sp, n_col, n_slice, 128)
+
+
+def test_traffic_inter_formula():
+    # 2 nodes x 2 ranks; rank 0's inter traffic: tiles owned by rank 2 (same position, other node)
+    remap = np.array([0, 1, 2, 3, 2])
+    sp = np.array([0, 0, 1, 0, 0])
+    n_col = np.array([1, 1, 10, 1, 3])
+    n_slice = np.array([5, 5, 50, 5, 7])
+    assert planner.traffic_inter(0, 2, 2, remap, sp, n_col, n_slice, 4) == 4 * 4 * (10 + 7)
+    assert planner.traffic_inter(0, 2, 1, remap, sp, n_col, n_slice, 4) == 0
+
+
+def test_gflops_formula():
+    assert planner.gflops(1_000_000, 128, 2.0) == pytest.approx(2.0 * 1e6 * 128 / 2.0 / 1e6)
+
+
+def test_alloc_slice_and_random():
+    assert planner.alloc_slice(4, 3).tolist() == [0, 0, 0, 1, 1, 1, 2, 2, 2, 3, 3, 3]
+    r = planner.alloc_random(8, 4, seed=9)
+    assert sorted(r.tolist()) == sorted(planner.alloc_slice(8, 4).tolist())
+    assert (r == planner.alloc_random(8, 4, seed=9)).all()

@@ -1,0 +1,123 @@
+"""Parity of the sm_100a SpMM kernels (through the C ABI) with the CPU oracle.
+
+Tolerance (fp32, from the engine's specification): elementwise
+    |C_gpu - C_ref| <= 1e-5 * (|A|.|B|)
+where C_ref is the double-accumulated CSR x dense product of the same fp32 inputs.
+"""
+import numpy as np
+import pytest
+
+import distspmm_b200 as d
+import oracle
+
+pytestmark = pytest.mark.gpu
+RTOL = 1e-5
+
+
+def _run(A, N, seed=3, accumulate=False, C0=None, dims_hint=None):
+    import torch
+    from distspmm_b200.spmm import SpmmPlan
+    B = d.dense_b(A.num_cols, N, seed)
+    plan = SpmmPlan(A, 0, dims_hint or N)
+    Bt = torch.from_numpy(B).cuda()
+    Ct = torch.from_numpy(C0).cuda() if C0 is not None else None
+    C = plan(Bt, Ct, accumulate=accumulate)
+    torch.cuda.synchronize()
+    return B, C.cpu().numpy(), plan
+
+
+def _check(A, B, C, C0=None):
+    ref, ab = oracle.spmm_f64(A.indptr, A.indices, A.values, B)
+    if C0 is not None:
+        ref = ref + C0
+        ab = ab + np.abs(C0)
+    ok, worst = oracle.check_close(C, ref, ab, RTOL)
+    assert np.isfinite(C).all()
+    assert ok, f"worst |dC| / (1e-5 |A||B|) = {worst:.3f}"
+    return worst
+
+
+@pytest.fixture(scope="module")
+def rmat13():
+    return d.gen_rmat(13, seed=2)
+
+
+@pytest.mark.parametrize("N", [1, 3, 4, 8, 16, 32, 64, 96, 100, 128, 256, 384, 512, 640])
+def test_rmat_widths(gpu, rmat13, N):
+    B, C, plan = _run(rmat13, N)
+    info = plan.info()
+    assert info["pieces"] > 0  # the hub rows of R-MAT are split into pieces
+    _check(rmat13, B, C)
+
+
+@pytest.mark.parametrize("kind,kw,N", [
+    ("rmat", dict(scale=15), 32),   # configuration 1 of the benchmark set
+    ("stencil27", dict(n=24), 128),
+    ("uniform", dict(rows=1 << 14, nnz_per_row=32), 256),
+])
+def test_matrix_families(gpu, kind, kw, N):
+    A = d.make_matrix(kind, seed=4, **kw)
+    B, C, _ = _run(A, N)
+    _check(A, B, C)
+
+
+def test_accumulate(gpu, rmat13):
+    C0 = d.dense_b(rmat13.num_rows, 128, seed=77)
+    B, C, _ = _run(rmat13, 128, accumulate=True, C0=C0.copy())
+    _check(rmat13, B, C, C0)
+
+
+def test_deterministic(gpu, rmat13):
+    _, C1, _ = _run(rmat13, 128)
+    _, C2, _ = _run(rmat13, 128)
+    assert np.array_equal(C1, C2)  # fixed summation order, no atomics
+
+
+def test_strided_and_unaligned_operands(gpu, rmat13):
+    """B and C as column windows of wider buffers (ld > N, not 16-byte aligned: the
+    scalar kernel path)."""
+    import torch
+    from distspmm_b200.spmm import SpmmPlan
+    N = 64
+    Bw = d.dense_b(rmat13.num_cols, N + 3, seed=5)
+    plan = SpmmPlan(rmat13, 0, N)
+    Bt = torch.from_numpy(Bw).cuda()
+    Cw = torch.full((rmat13.num_rows, N + 5), 7.0, device="cuda")
+    plan(Bt[:, 1:N + 1], Cw[:, 2:N + 2])
+    torch.cuda.synchronize()
+    C = Cw.cpu().numpy()
+    assert (C[:, :2] == 7).all() and (C[:, N + 2:] == 7).all()  # nothing written outside the window
+    _check(rmat13, np.ascontiguousarray(Bw[:, 1:N + 1]), C[:, 2:N + 2])
+
+
+def test_edge_cases(gpu):
+    import torch
+    from distspmm_b200.spmm import SpmmPlan
+    # all rows empty
+    E = d.Csr(np.zeros(11, np.int64), np.zeros(0, np.int64), np.zeros(0, np.float32), 10, 10)
+    B, C, _ = _run(E, 32)
+    assert (C == 0).all()
+    # one huge row (forces many pieces) among empty rows, and a single-row matrix
+    n = 200_000
+    idx = np.arange(n, dtype=np.int64)
+    H = d.Csr(np.array([0, 0, n, n], np.int64), idx, np.random.default_rng(1).random(n).astype(np.float32), 3, n)
+    B, C, plan = _run(H, 128)
+    assert plan.info()["pieces"] >= n // plan.info()["piece_cap"]
+    _check(H, B, C)
+    R = d.Csr(np.array([0, 3], np.int64), np.array([0, 1, 2], np.int64), np.ones(3, np.float32), 1, 3)
+    B, C, _ = _run(R, 5)
+    _check(R, B, C)
+    # zero-width B
+    plan = SpmmPlan(R, 0, 4)
+    plan(torch.zeros((3, 0), device="cuda"))
+
+
+def test_reference_run_mode_b_all_ones(gpu):
+    """The reference runs with B = 1 (src/dist_spmm_node.cu:192): C[i,:] = row sum of A."""
+    import torch
+    from distspmm_b200.spmm import SpmmPlan
+    A = d.gen_stencil27(16, seed=9)
+    plan = SpmmPlan(A, 0, 128)
+    C = plan(torch.ones((A.num_cols, 128), device="cuda")).cpu().numpy()
+    rs = np.add.reduceat(A.values.astype(np.float64), A.indptr[:-1])
+    assert np.allclose(C, rs[:, None], rtol=0, atol=1e-5 * 52)
