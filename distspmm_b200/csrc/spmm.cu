@@ -418,9 +418,11 @@ extern "C" int dsp_spmm_plan_info(const dsp_spmm_plan *p, dsp_spmm_info *info) {
 
 extern "C" int dsp_spmm_f32(dsp_spmm_plan *p, const float *B, int64_t ldb, float *C, int64_t ldc, int N,
                             int accumulate, void *stream) {
-  DSP_TRY_ARG(p && (B || p->op.nnz == 0) && (C || p->op.rows == 0), "dsp_spmm_f32: null argument");
+  DSP_TRY_ARG(p, "dsp_spmm_f32: null plan");
   DSP_TRY_ARG(N >= 0 && ldb >= N && ldc >= N, "dsp_spmm_f32: N=%d ldb=%lld ldc=%lld", N, (long long)ldb,
               (long long)ldc);
+  if (N == 0) return DSP_OK;  // nothing to compute; empty operands may be null
+  DSP_TRY_ARG((B || p->op.nnz == 0) && (C || p->op.rows == 0), "dsp_spmm_f32: null argument");
   if (p->op.pieces > 0 && p->op.pieces * (int64_t)N > p->scratch_floats) {
     // first use with a wider B than the plan was sized for: grow the scratch (synchronous)
     cudaSetDevice(p->op.device);
