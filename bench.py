@@ -49,7 +49,12 @@ def parse_args(argv=None):
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--scale", type=int, default=20)
+    ap.add_argument("--matrix", choices=["rmat", "stencil27", "uniform"], default="rmat",
+                    help="rmat: configurations 1/2/5; stencil27: configuration 3; uniform: configuration 4")
+    ap.add_argument("--scale", type=int, default=20, help="R-MAT scale")
+    ap.add_argument("--grid", type=int, default=160, help="stencil grid edge (160 -> 4,096,000 rows)")
+    ap.add_argument("--rows", type=int, default=1 << 22, help="uniform matrix rows")
+    ap.add_argument("--nnz-per-row", type=int, default=32, help="uniform matrix nonzeros per row")
     ap.add_argument("--dims", type=int, default=128)
     ap.add_argument("--n-rolls", type=int, default=4)
     ap.add_argument("--task-dist", type=int, default=2)
@@ -69,16 +74,36 @@ def env_rank():
 
 
 def workload_name(a):
+    if a.matrix == "stencil27":
+        return f"stencil{a.grid}_n{a.dims}"
+    if a.matrix == "uniform":
+        return f"uniform{a.rows}x{a.nnz_per_row}_n{a.dims}"
     return f"rmat{a.scale}_n{a.dims}"
 
 
+def matrix_desc(a):
+    if a.matrix == "stencil27":
+        return f"27-point stencil on a {a.grid}^3 grid, lexicographic; diagonal 26, off-diagonals U(-1,0)"
+    if a.matrix == "uniform":
+        return f"uniform random {a.rows} x {a.rows}, {a.nnz_per_row} distinct columns per row, values U(0,1)"
+    return f"R-MAT scale {a.scale}, ef 16, (.57,.19,.19,.05), symmetrised, dedup, no self-loops, values U(0,1)"
+
+
+def make_workload(a):
+    import distspmm_b200 as d
+    if a.matrix == "stencil27":
+        return d.gen_stencil27(a.grid, seed=a.seed)
+    if a.matrix == "uniform":
+        return d.gen_uniform(a.rows, a.nnz_per_row, seed=a.seed)
+    return d.gen_rmat(a.scale, seed=a.seed)
+
+
 def config_of(a, world, nnz, M):
-    return {"workload": workload_name(a),
-            "matrix": f"R-MAT scale {a.scale}, ef 16, (.57,.19,.19,.05), symmetrised, dedup, no self-loops",
+    return {"workload": workload_name(a), "matrix": matrix_desc(a),
             "rows": M, "nnz": nnz, "dims": a.dims, "n_rolls": a.n_rolls, "task_dist": a.task_dist,
             "comm_type": a.comm_type, "parallelism": f"row1d_p{world}", "seed": a.seed,
             "l2": "flushed between steps (512 MiB write)" if not a.no_flush else "not flushed",
-            "b": "U(-1,1) fp32 row-major", "values": "U(0,1) fp32"}
+            "b": "U(-1,1) fp32 row-major"}
 
 
 def measured_peaks():
@@ -179,7 +204,7 @@ def run_reference(a, rank, world):
     if rank != 0:
         return 0
     import distspmm_b200 as d
-    A = d.gen_rmat(a.scale, seed=a.seed)
+    A = make_workload(a)
     B = d.dense_b(A.num_cols, a.dims, seed=a.seed + 1)
     import numpy as np
 
@@ -239,7 +264,7 @@ def main(argv=None):
         comm = TorchComm()
 
     # every rank builds the whole matrix (the reference: every rank reads the whole file)
-    A = d.gen_rmat(a.scale, seed=a.seed)
+    A = make_workload(a)
     M, nnz = A.num_rows, A.nnz
     lb, ub = planner.partition_bounds(M, world, rank)
     local = planner.partition(A, lb, ub)

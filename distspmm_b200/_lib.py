@@ -46,7 +46,7 @@ class dsp_comm_model(ctypes.Structure):
 
 
 class dsp_spmm_info(ctypes.Structure):
-    _fields_ = [(n, c_i64) for n in ("rows", "cols", "nnz", "items", "split_rows", "pieces",
+    _fields_ = [(n, c_i64) for n in ("rows", "cols", "nnz", "variant", "items", "split_rows", "pieces",
                                      "piece_cap", "max_row_len", "scratch_bytes", "device_bytes")]
 
 
@@ -109,7 +109,7 @@ PROTOTYPES = {
     "dsp_traffic_inter": (c_int, [c_int, c_int, c_int, c_int, P(c_i32), P(ctypes.c_uint8), P(c_i32),
                                   P(c_i32), c_int, P(c_i64)]),
     "dsp_gflops": (c_f64, [c_i64, c_int, c_f64]),
-    "dsp_spmm_plan_create": (c_int, [c_int, P(dsp_csr), c_int, P(c_vp)]),
+    "dsp_spmm_plan_create": (c_int, [c_int, P(dsp_csr), c_int, c_int, P(c_vp)]),
     "dsp_spmm_plan_destroy": (None, [c_vp]),
     "dsp_spmm_plan_info": (c_int, [c_vp, P(dsp_spmm_info)]),
     "dsp_spmm_f32": (c_int, [c_vp, c_vp, c_i64, c_vp, c_i64, c_int, c_int, c_vp]),

@@ -9,11 +9,27 @@ namespace dsp {
 
 constexpr int kSpmmThreads = 256;
 
+// The two SpMM work decompositions (picked per operand from its row-length statistics).
+enum SpmmVariant : int {
+  kRowSplit = 0,  // one item per row (heavy rows cut into pieces): regular, short-tailed rows
+  kNnzSplit = 1,  // equal nonzero chunks across row boundaries (merge-path style): skewed rows
+};
+
 // Arguments of one SpMM launch (passed by value to the kernels).
 struct SpmmArgs {
+  int variant;
+  // row-split
   const int64_t *item_ptr;  // [n_items + 1]
   const int32_t *item_out;  // [n_items]  row (>= 0) or -(slot + 1)
   int64_t n_items;
+  // nnz-split
+  const int32_t *coo_row;     // [nnz] output row of each nonzero
+  const int32_t *chunk_slot;  // [2 * n_chunks] partial slot of the head / tail row, -1 if whole
+  int64_t n_chunks;
+  int64_t chunk_nnz;
+  int64_t nnz;
+  int64_t zero_rows;  // rows [0, zero_rows) without nonzeros are written as 0 (non-accumulating)
+  // both: rows cut across items / chunks, summed into C by the fixup kernel
   const int32_t *split_row;  // [n_split]
   const int32_t *split_ptr;  // [n_split + 1] slot ranges
   int64_t n_split;
@@ -23,19 +39,19 @@ struct SpmmArgs {
   int64_t ldb;
   float *C;
   int64_t ldc;
-  float *partial;  // [pieces][N]
+  float *partial;  // [slots][N]
   int N;
 };
 
 struct SpmmShape {
   int W;           // floats per vector (4 or 1)
-  int LPR;         // lanes per item
+  int LPR;         // lanes per item / chunk
   int VPL;         // vectors per lane
   int chunk_cols;  // columns per blockIdx.y
   int chunks;
 };
 
-SpmmShape spmm_shape(int N, const float *B, int64_t ldb, const float *C, int64_t ldc);
+SpmmShape spmm_shape(int N, int variant, const float *B, int64_t ldb, const float *C, int64_t ldc);
 int launch_spmm(const SpmmArgs &a, bool accumulate, cudaStream_t stream);
 int launch_fill_dense(float *B, int64_t row0, int64_t rows, int64_t ld, int64_t ncols, uint64_t seed,
                       cudaStream_t stream);
@@ -43,13 +59,18 @@ int launch_fill_const(float *B, int64_t n, float v, cudaStream_t stream);
 void prefer_l1_carveout();
 int dev_upload(void *dptr_out, const void *host, size_t bytes);
 
-// A CSR operand in device memory, cut into work items.
+// A CSR operand in device memory, cut into work items (row-split) or nonzero chunks
+// (nnz-split).
 struct DevOperand {
   int device = 0;
+  int variant = kRowSplit;
   int64_t rows = 0, cols = 0, nnz = 0;
-  int64_t n_items = 0, n_split = 0, pieces = 0, piece_cap = 0, max_row_len = 0;
+  int64_t n_items = 0, n_chunks = 0, chunk_nnz = 0, n_split = 0, pieces = 0, piece_cap = 0, max_row_len = 0;
+  int64_t zero_rows = 0;
   int64_t *d_item_ptr = nullptr;
   int32_t *d_item_out = nullptr;
+  int32_t *d_coo_row = nullptr;
+  int32_t *d_chunk_slot = nullptr;
   int32_t *d_split_row = nullptr;
   int32_t *d_split_ptr = nullptr;
   int32_t *d_cols = nullptr;
@@ -57,10 +78,14 @@ struct DevOperand {
 
   // Rows i < m with nonzeros [row_ptr[i], row_ptr[i+1]) of indices/values (offsets are
   // absolute; first_nz is subtracted); row_ids[i] is the output row (nullptr = i).
+  // include_empty: the operand writes every output row [0, rows) (non-accumulating use).
+  // dims: the dense width it is tuned for; variant < 0 picks from the row statistics.
   int upload(int device, int64_t rows, int64_t cols, const int64_t *row_ptr, const int32_t *row_ids, int64_t m,
-             const int64_t *indices, const float *values, int64_t first_nz, int64_t nnz, int64_t piece_cap,
-             bool include_empty);
+             const int64_t *indices, const float *values, int64_t first_nz, int64_t nnz, int dims,
+             bool include_empty, int variant = -1);
   void release();
+  // work units a launch covers: row items (row-split) or nonzero chunks (nnz-split)
+  int64_t units() const { return variant == kRowSplit ? n_items : n_chunks; }
   int64_t device_bytes() const;
   SpmmArgs args(const float *B, int64_t ldb, float *C, int64_t ldc, int N, float *partial) const;
 };

@@ -3,6 +3,7 @@
 // bulk/sparse selector and the traffic formulas; plus the work-item builder of the SpMM
 // kernels.
 #include <math.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include "internal.h"
@@ -411,6 +412,92 @@ void build_items(int64_t m, const int32_t *rows, const int64_t *row_ptr, int64_t
   out->item_ptr.push_back(m > 0 ? row_ptr[m] : 0);
   // an item list that skipped trailing empty rows still ends at the last nonzero
   out->pieces = slots;
+}
+
+int64_t default_chunk_nnz(int dims, int64_t nnz) {
+  static const int64_t forced = [] {
+    const char *e = getenv("DSP_SPMM_CHUNK");
+    return e ? (int64_t)atoll(e) : 0;
+  }();
+  if (forced > 0) return (forced + 31) & ~int64_t(31);
+  // about 32K multiply-adds per chunk (256 nonzeros at N = 128) ...
+  int64_t c = 32768 / std::max(dims, 1);
+  c = std::max<int64_t>(32, std::min<int64_t>(c, 1024));
+  // ... but at least ~16K chunks (enough lane groups for every SM) when the matrix allows
+  const int64_t min_chunks = 16384;
+  if (nnz / c < min_chunks) c = std::max<int64_t>(32, nnz / min_chunks);
+  return (c + 31) & ~int64_t(31);
+}
+
+void build_chunks(int64_t m, const int32_t *rows, const int64_t *row_ptr, int64_t chunk_nnz, ChunkPlan *out) {
+  const int64_t nnz = m > 0 ? row_ptr[m] : 0;
+  out->chunk_nnz = chunk_nnz;
+  out->n_chunks = (nnz + chunk_nnz - 1) / chunk_nnz;
+  out->coo_row.assign((size_t)std::max<int64_t>(nnz, 1), 0);
+  out->chunk_slot.assign((size_t)std::max<int64_t>(2 * out->n_chunks, 1), -1);
+  out->split_row.clear();
+  out->split_ptr.assign(1, 0);
+  std::atomic<int64_t> maxlen{0};
+  parallel_for(m, [&](int64_t b, int64_t e) {
+    int64_t ml = 0;
+    for (int64_t i = b; i < e; ++i) {
+      const int32_t r = rows ? rows[i] : (int32_t)i;
+      for (int64_t p = row_ptr[i]; p < row_ptr[i + 1]; ++p) out->coo_row[(size_t)p] = r;
+      ml = std::max(ml, row_ptr[i + 1] - row_ptr[i]);
+    }
+    int64_t cur = maxlen.load();
+    while (ml > cur && !maxlen.compare_exchange_weak(cur, ml)) {
+    }
+  }, 4096);
+  out->max_row_len = maxlen.load();
+  // index of the (nonempty) row holding nonzero p
+  auto row_of = [&](int64_t p) { return (int64_t)(std::upper_bound(row_ptr, row_ptr + m + 1, p) - row_ptr) - 1; };
+  int64_t last_idx = -1;
+  int32_t slots = 0;
+  auto add_slot = [&](int64_t idx) {
+    if (idx != last_idx) {
+      out->split_row.push_back(rows ? rows[idx] : (int32_t)idx);
+      out->split_ptr.push_back(slots);
+      last_idx = idx;
+    }
+    out->split_ptr.back() = ++slots;
+    return slots - 1;
+  };
+  for (int64_t c = 0; c < out->n_chunks; ++c) {
+    const int64_t s = c * chunk_nnz, e = std::min(s + chunk_nnz, nnz);
+    const int64_t hr = row_of(s), tr = row_of(e - 1);
+    const bool head_cut = row_ptr[hr] < s;        // the row began in an earlier chunk
+    const bool tail_cut = row_ptr[tr + 1] > e;    // the row goes on in a later chunk
+    if (hr == tr) {
+      if (head_cut || tail_cut) out->chunk_slot[(size_t)(2 * c)] = out->chunk_slot[(size_t)(2 * c + 1)] = add_slot(hr);
+    } else {
+      if (head_cut) out->chunk_slot[(size_t)(2 * c)] = add_slot(hr);
+      if (tail_cut) out->chunk_slot[(size_t)(2 * c + 1)] = add_slot(tr);
+    }
+  }
+  out->slots = slots;
+}
+
+int choose_variant(int64_t m, const int64_t *row_ptr, int dims) {
+  static const int forced = [] {
+    const char *e = getenv("DSP_SPMM_VARIANT");
+    if (!e) return -1;
+    return strcmp(e, "rows") == 0 ? 0 : strcmp(e, "nnz") == 0 ? 1 : -1;
+  }();
+  if (forced >= 0) return forced;
+  (void)dims;
+  // Row-split keeps one row per warp: good when rows are long enough to keep several
+  // B-row loads in flight and of similar length; otherwise chunks of equal nonzeros.
+  int64_t nonempty = 0, maxlen = 0, nnz = m > 0 ? row_ptr[m] : 0;
+  for (int64_t i = 0; i < m; ++i) {
+    const int64_t len = row_ptr[i + 1] - row_ptr[i];
+    nonempty += len > 0;
+    maxlen = std::max(maxlen, len);
+  }
+  if (nonempty == 0) return 0;
+  const double mean = (double)nnz / (double)nonempty;
+  const double empty_frac = 1.0 - (double)nonempty / (double)m;
+  return (mean >= 16.0 && (double)maxlen <= 4.0 * mean && empty_frac < 0.05) ? 0 : 1;
 }
 
 }  // namespace dsp

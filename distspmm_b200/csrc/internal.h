@@ -50,6 +50,31 @@ int64_t default_piece_cap(int dims);
 void build_items(int64_t m, const int32_t *rows, const int64_t *row_ptr, int64_t piece_cap,
                  bool include_empty, ItemPlan *out);
 
+// Equal nonzero chunks for the nnz-split kernels:
+//   coo_row[p]           output row of nonzero p
+//   chunk_slot[2c+0/1]   partial slot of chunk c's first / last row when that row crosses a
+//                        chunk boundary, -1 when the chunk holds the whole row
+//   split_row/split_ptr  rows crossing boundaries and their consecutive slots (chunk order)
+struct ChunkPlan {
+  std::vector<int32_t> coo_row;
+  std::vector<int32_t> chunk_slot;
+  std::vector<int32_t> split_row;
+  std::vector<int32_t> split_ptr;
+  int64_t chunk_nnz = 0;
+  int64_t n_chunks = 0;
+  int64_t slots = 0;
+  int64_t max_row_len = 0;
+};
+
+// Nonzeros per chunk for a dense width (about 32K multiply-adds per chunk, fewer when the
+// matrix is too small to give every SM enough chunks).
+int64_t default_chunk_nnz(int dims, int64_t nnz);
+
+void build_chunks(int64_t m, const int32_t *rows, const int64_t *row_ptr, int64_t chunk_nnz, ChunkPlan *out);
+
+// Row-length statistics -> kRowSplit (0) for short, regular rows, kNnzSplit (1) otherwise.
+int choose_variant(int64_t m, const int64_t *row_ptr, int dims);
+
 }  // namespace dsp
 
 #define DSP_TRY_ARG(cond, ...)                          \

@@ -153,7 +153,6 @@ int build_segments(dsp_rank *r, const dsp_csr *a) {
   const int64_t m = a->num_rows, cpt = r->cpt;
   auto seg_of = [&](int64_t c) { return (r->remap[(size_t)(c / cpt)] - me + P) % P; };
   r->segs.resize((size_t)P);
-  const int64_t piece_cap = default_piece_cap(r->dims);
   for (int k = 0; k < P; ++k) {
     auto &S = r->segs[(size_t)k];
     S.owner = (me + k) % P;
@@ -188,7 +187,7 @@ int build_segments(dsp_rank *r, const dsp_csr *a) {
       }
     }, 1024);
     int rc = S.op.upload(r->device, m, r->M, ptr.data(), k == 0 ? nullptr : rows.data(), nr, idx.data(),
-                         val.data(), 0, nz, piece_cap, k == 0);
+                         val.data(), 0, nz, r->dims, k == 0);
     if (rc) return rc;
     r->scratch_floats = std::max(r->scratch_floats, S.op.pieces * (int64_t)r->dims);
   }
@@ -310,9 +309,9 @@ extern "C" int dsp_rank_create(const dsp_rank_desc *d, dsp_rank **out) {
   s.launches_per_step = 0;
   for (int k = 0; k < r->P; ++k) {
     const auto &op = r->segs[(size_t)k].op;
-    if (k == 0 || op.n_items > 0) {
+    if (k == 0 || op.units() > 0) {
       s.segments++;
-      s.kernels_per_step += (op.n_items > 0) + (op.n_split > 0);
+      s.kernels_per_step += (op.units() > 0) + (op.n_split > 0);
     }
     if (k > 0) {
       s.kernels_per_step += r->fetch[(size_t)k].n_rows > 0;
@@ -494,7 +493,7 @@ extern "C" int dsp_rank_step(dsp_rank *r, void *stream_v) {
   DSP_CUDA(cudaEventRecord(r->ev_c0, r->compute));
   for (int k = 0; k < r->P; ++k) {
     const auto &op = r->segs[(size_t)k].op;
-    if (k > 0 && op.n_items == 0) continue;
+    if (k > 0 && op.units() == 0) continue;
     if (has_fetch[(size_t)k]) DSP_CUDA(cudaStreamWaitEvent(r->compute, r->ev_fetch[(size_t)k], 0));
     int rc = launch_spmm(op.args(r->B, r->dims, r->C, r->dims, r->dims, r->scratch), k > 0, r->compute);
     if (rc) return rc;

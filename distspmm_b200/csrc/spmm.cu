@@ -1,22 +1,29 @@
 // spmm.cu — sm_100a CSR x dense fp32 SpMM kernels and the single-GPU plan API.
 //
 // C[rows x N] (+)= A[rows x cols] * B[cols x N]; A in CSR with int32 column ids, B and C
-// row-major fp32. This is a gather-and-accumulate, bound by HBM / L2 bandwidth, not a
-// dense contraction, so it runs on the CUDA cores:
-//   * the rows are cut on the host into work items: one item per row, except rows longer
-//     than `piece_cap` nonzeros, which become balanced pieces whose partial rows go to a
-//     scratch buffer and are summed in piece order by a fixup kernel (deterministic; no
-//     atomics);
-//   * a group of LPR lanes (a warp for N >= 128) owns one item; each lane holds VPL
-//     vectors of W floats of the output row, so one B row is read as LPR*W*4 contiguous
-//     bytes (512 B at N = 128: 32 lanes x float4);
-//   * the group loads LPR (column, value) pairs with one coalesced streaming load each,
-//     broadcasts them with warp shuffles, and keeps up to 8 B-row loads in flight per lane
-//     before the FMAs;
-//   * B goes through the read-only path (L1-cached: rows shared by neighbouring items hit
-//     in L1), A is streamed (evict-first), whole-row results are stored once.
+// row-major fp32. This is a gather-and-accumulate bound by L2 / HBM bandwidth and by the
+// number of B-row loads in flight, not a dense contraction, so it runs on the CUDA cores.
+//
+// Two work decompositions, picked per operand from its row-length statistics:
+//   row-split  one item per row; rows longer than `piece_cap` nonzeros are cut into
+//              balanced pieces. Good for regular rows (stencils, fixed-degree rows).
+//   nnz-split  equal chunks of `chunk_nnz` consecutive nonzeros per lane group regardless
+//              of row boundaries (merge-path style): every group keeps the same number of
+//              B-row loads in flight even when rows hold 1-3 nonzeros (R-MAT). Rows are
+//              flushed as the chunk crosses them; rows cut by a chunk boundary write
+//              partial rows to slots.
+// In both, partial rows are summed in a fixed order by a fixup kernel (deterministic, no
+// atomics), so repeated runs are bit-identical.
+//
+// Per group of LPR lanes (a warp for N >= 128) each lane holds VPL vectors of W floats of
+// the output row, so one B row is read as LPR*W*4 contiguous bytes (512 B at N = 128:
+// 32 lanes x float4). (column, value[, row]) triples are loaded once per lane per 32
+// nonzeros with streaming loads and broadcast by warp shuffles; B rows go through the
+// read-only path with an L2 evict_last policy (A and C stream past them); final C rows
+// are written once with streaming stores.
 // Replaces cusparseSpMM(COO, ALG_DEFAULT, beta = 1) of src/dist_spmm_node.cu:354-385.
 #include <cuda_runtime.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include "device.cuh"
@@ -31,9 +38,18 @@ template <>
 struct Vec<4> {
   using T = float4;
   static __device__ __forceinline__ T zero() { return make_float4(0.f, 0.f, 0.f, 0.f); }
-  static __device__ __forceinline__ T ldg(const float *p) { return __ldg(reinterpret_cast<const float4 *>(p)); }
+  // B rows: read-only path, kept in L2 ahead of the streamed A and C (evict_last policy)
+  static __device__ __forceinline__ T ldg(const float *p, uint64_t pol) {
+    T v;
+    asm("ld.global.nc.L2::cache_hint.v4.f32 {%0,%1,%2,%3}, [%4], %5;"
+        : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+        : "l"(p), "l"(pol));
+    return v;
+  }
   static __device__ __forceinline__ T ld(const float *p) { return *reinterpret_cast<const float4 *>(p); }
   static __device__ __forceinline__ void st(float *p, T v) { *reinterpret_cast<float4 *>(p) = v; }
+  // final C rows are not re-read by this kernel: streaming store, no L2 residency
+  static __device__ __forceinline__ void st_stream(float *p, T v) { __stcs(reinterpret_cast<float4 *>(p), v); }
   static __device__ __forceinline__ void fma(T &acc, float s, T b) {
     acc.x = fmaf(s, b.x, acc.x);
     acc.y = fmaf(s, b.y, acc.y);
@@ -51,87 +67,225 @@ template <>
 struct Vec<1> {
   using T = float;
   static __device__ __forceinline__ T zero() { return 0.f; }
-  static __device__ __forceinline__ T ldg(const float *p) { return __ldg(p); }
+  static __device__ __forceinline__ T ldg(const float *p, uint64_t) { return __ldg(p); }
   static __device__ __forceinline__ T ld(const float *p) { return *p; }
   static __device__ __forceinline__ void st(float *p, T v) { *p = v; }
+  static __device__ __forceinline__ void st_stream(float *p, T v) { __stcs(p, v); }
   static __device__ __forceinline__ void fma(T &acc, float s, T b) { acc = fmaf(s, b, acc); }
   static __device__ __forceinline__ void add(T &acc, T b) { acc += b; }
 };
 
-// ------------------------------------------------------------------ kernels
+__device__ __forceinline__ uint64_t evict_last_policy() {
+  uint64_t pol;
+  asm("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
 
-// One item per group of LPR lanes; blockIdx.y selects a chunk of LPR*VPL*W columns.
+template <int LPR>
+__device__ __forceinline__ unsigned group_mask() {
+  return LPR == 32 ? 0xffffffffu : (((1u << LPR) - 1u) << ((threadIdx.x & 31) & ~(LPR - 1)));
+}
+
+// nonzeros whose B vectors are loaded before their FMAs: about 8 vectors in flight per
+// lane (never more nonzeros than one shuffle round holds)
+template <int LPR, int VPL>
+__host__ __device__ constexpr int loads_in_flight() {
+  return (8 / VPL < 1 ? 1 : 8 / VPL) < LPR ? (8 / VPL < 1 ? 1 : 8 / VPL) : LPR;
+}
+
+// (column, value[, row]) entries each lane loads per round: one round covers up to 32
+// nonzeros of the group, so the streamed A loads are issued together
+template <int LPR>
+__host__ __device__ constexpr int entries_per_lane() {
+  return 32 / LPR < 8 ? 32 / LPR : 8;
+}
+
+// Write one output row held in acc: to its partial slot, or to C (adding C when
+// accumulating). col0 is this lane's first column.
 template <int LPR, int VPL, int W, bool kAccum>
-__global__ void __launch_bounds__(kSpmmThreads) spmm_items_kernel(const SpmmArgs a) {
+__device__ __forceinline__ void flush_row(const SpmmArgs &a, int32_t row, int32_t slot, int col0,
+                                          const typename Vec<W>::T (&acc)[VPL]) {
   using V = Vec<W>;
   using T = typename V::T;
-  // nonzeros whose B vectors are loaded before their FMAs: 8 vectors in flight per lane
-  constexpr int U = LPR < 8 ? LPR : (8 / VPL >= 2 ? 8 / VPL : 2);
-  const int lane = threadIdx.x & (LPR - 1);
-  const int64_t item = ((int64_t)blockIdx.x * kSpmmThreads + threadIdx.x) / LPR;
-  if (item >= a.n_items) return;
-  const unsigned gmask =
-      LPR == 32 ? 0xffffffffu : (((1u << LPR) - 1u) << ((threadIdx.x & 31) & ~(LPR - 1)));
-  const int col0 = blockIdx.y * (LPR * VPL * W) + lane * W;
-  const int64_t beg = a.item_ptr[item], end = a.item_ptr[item + 1];
-
-  T acc[VPL];
+  if (slot >= 0) {
+    float *dst = a.partial + (int64_t)slot * a.N;
 #pragma unroll
-  for (int w = 0; w < VPL; ++w) acc[w] = V::zero();
-
-  for (int64_t base = beg; base < end; base += LPR) {
-    const int n = (int)min((int64_t)LPR, end - base);
-    int c = 0;
-    float v = 0.f;
-    if (lane < n) {
-      c = __ldcs(a.cols + base + lane);
-      v = __ldcs(a.vals + base + lane);
+    for (int w = 0; w < VPL; ++w) {
+      const int col = col0 + w * LPR * W;
+      if (col < a.N) V::st(dst + col, acc[w]);
     }
-    for (int j = 0; j < n; j += U) {
-      T b[U][VPL];
-      float s[U];
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int cj = __shfl_sync(gmask, c, j + u, LPR);
-        s[u] = __shfl_sync(gmask, v, j + u, LPR);
-        const float *brow = a.B + (int64_t)cj * a.ldb;
-#pragma unroll
-        for (int w = 0; w < VPL; ++w) {
-          const int col = col0 + w * LPR * W;
-          b[u][w] = (j + u < n && col < a.N) ? V::ldg(brow + col) : V::zero();
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < U; ++u)
-#pragma unroll
-        for (int w = 0; w < VPL; ++w)
-          if (j + u < n) V::fma(acc[w], s[u], b[u][w]);
-    }
-  }
-
-  const int32_t o = a.item_out[item];
-  if (o >= 0) {
-    float *dst = a.C + (int64_t)o * a.ldc;
+  } else {
+    float *dst = a.C + (int64_t)row * a.ldc;
 #pragma unroll
     for (int w = 0; w < VPL; ++w) {
       const int col = col0 + w * LPR * W;
       if (col < a.N) {
         T r = acc[w];
         if (kAccum) V::add(r, V::ld(dst + col));
-        V::st(dst + col, r);
+        V::st_stream(dst + col, r);
       }
-    }
-  } else {
-    float *dst = a.partial + (int64_t)(-(o + 1)) * a.N;
-#pragma unroll
-    for (int w = 0; w < VPL; ++w) {
-      const int col = col0 + w * LPR * W;
-      if (col < a.N) V::st(dst + col, acc[w]);
     }
   }
 }
 
-// One warp per split row: C[row] = (kAccum ? C[row] : 0) + sum of its pieces, in order.
+// Rows [r0, r1) hold no nonzeros: write their zeros (non-accumulating launches only).
+template <int LPR, int VPL, int W>
+__device__ __forceinline__ void zero_rows(const SpmmArgs &a, int64_t r0, int64_t r1, int col0) {
+  using V = Vec<W>;
+  for (int64_t r = r0; r < r1; ++r) {
+    float *dst = a.C + r * a.ldc;
+#pragma unroll
+    for (int w = 0; w < VPL; ++w) {
+      const int col = col0 + w * LPR * W;
+      if (col < a.N) V::st_stream(dst + col, V::zero());
+    }
+  }
+}
+
+// ------------------------------------------------------------------ row-split kernel
+
+// One item per group of LPR lanes; blockIdx.y selects a chunk of LPR*VPL*W columns.
+template <int LPR, int VPL, int W, bool kAccum>
+__global__ void __launch_bounds__(kSpmmThreads) spmm_rows_kernel(const SpmmArgs a) {
+  using V = Vec<W>;
+  using T = typename V::T;
+  constexpr int U = loads_in_flight<LPR, VPL>();
+  const int lane = threadIdx.x & (LPR - 1);
+  const int64_t item = ((int64_t)blockIdx.x * kSpmmThreads + threadIdx.x) / LPR;
+  if (item >= a.n_items) return;
+  const unsigned gmask = group_mask<LPR>();
+  const int col0 = blockIdx.y * (LPR * VPL * W) + lane * W;
+  const int64_t beg = a.item_ptr[item], end = a.item_ptr[item + 1];
+  const uint64_t pol = evict_last_policy();
+
+  constexpr int K = entries_per_lane<LPR>();
+  T acc[VPL];
+#pragma unroll
+  for (int w = 0; w < VPL; ++w) acc[w] = V::zero();
+
+  for (int64_t base = beg; base < end; base += LPR * K) {
+    int c[K];
+    float v[K];
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      const int64_t p = base + k * LPR + lane;
+      c[k] = p < end ? __ldcs(a.cols + p) : 0;
+      v[k] = p < end ? __ldcs(a.vals + p) : 0.f;
+    }
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      const int64_t kb = base + k * LPR;
+      if (kb >= end) break;
+      const int n = (int)min((int64_t)LPR, end - kb);
+      for (int j = 0; j < n; j += U) {
+        T b[U][VPL];
+        float s[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int cj = __shfl_sync(gmask, c[k], j + u, LPR);
+          s[u] = __shfl_sync(gmask, v[k], j + u, LPR);
+          const float *brow = a.B + (int64_t)cj * a.ldb;
+#pragma unroll
+          for (int w = 0; w < VPL; ++w) {
+            const int col = col0 + w * LPR * W;
+            b[u][w] = (j + u < n && col < a.N) ? V::ldg(brow + col, pol) : V::zero();
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+#pragma unroll
+          for (int w = 0; w < VPL; ++w)
+            if (j + u < n) V::fma(acc[w], s[u], b[u][w]);
+      }
+    }
+  }
+  const int32_t o = a.item_out[item];
+  flush_row<LPR, VPL, W, kAccum>(a, o, o >= 0 ? -1 : -(o + 1), col0, acc);
+}
+
+// ------------------------------------------------------------------ nnz-split kernel
+
+// One chunk of chunk_nnz consecutive nonzeros per group of LPR lanes.
+template <int LPR, int VPL, int W, bool kAccum>
+__global__ void __launch_bounds__(kSpmmThreads) spmm_nnz_kernel(const SpmmArgs a) {
+  using V = Vec<W>;
+  using T = typename V::T;
+  constexpr int U = loads_in_flight<LPR, VPL>();
+  const int lane = threadIdx.x & (LPR - 1);
+  const int64_t chunk = ((int64_t)blockIdx.x * kSpmmThreads + threadIdx.x) / LPR;
+  if (chunk >= a.n_chunks) return;
+  const unsigned gmask = group_mask<LPR>();
+  const int col0 = blockIdx.y * (LPR * VPL * W) + lane * W;
+  const int64_t s = chunk * a.chunk_nnz, e = min(s + a.chunk_nnz, a.nnz);
+  const int32_t head_slot = a.chunk_slot[2 * chunk], tail_slot = a.chunk_slot[2 * chunk + 1];
+  const uint64_t pol = evict_last_policy();
+
+  int32_t row = a.coo_row[s];
+  const int32_t head_row = row;
+  // empty rows between the previous chunk's last row and this chunk's first row
+  if (!kAccum) zero_rows<LPR, VPL, W>(a, s > 0 ? (int64_t)a.coo_row[s - 1] + 1 : 0, row, col0);
+
+  constexpr int K = entries_per_lane<LPR>();
+  T acc[VPL];
+#pragma unroll
+  for (int w = 0; w < VPL; ++w) acc[w] = V::zero();
+
+  for (int64_t base = s; base < e; base += LPR * K) {
+    int c[K], rr[K];
+    float v[K];
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      const int64_t p = base + k * LPR + lane;
+      c[k] = p < e ? __ldcs(a.cols + p) : 0;
+      v[k] = p < e ? __ldcs(a.vals + p) : 0.f;
+      rr[k] = p < e ? __ldcs(a.coo_row + p) : 0;
+    }
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      const int64_t kb = base + k * LPR;
+      if (kb >= e) break;
+      const int n = (int)min((int64_t)LPR, e - kb);
+      for (int j = 0; j < n; j += U) {
+        T b[U][VPL];
+        float sv[U];
+        int ru[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int cj = __shfl_sync(gmask, c[k], j + u, LPR);
+          sv[u] = __shfl_sync(gmask, v[k], j + u, LPR);
+          ru[u] = __shfl_sync(gmask, rr[k], j + u, LPR);
+          const float *brow = a.B + (int64_t)cj * a.ldb;
+#pragma unroll
+          for (int w = 0; w < VPL; ++w) {
+            const int col = col0 + w * LPR * W;
+            b[u][w] = (j + u < n && col < a.N) ? V::ldg(brow + col, pol) : V::zero();
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          if (j + u < n) {
+            if (ru[u] != row) {  // group-uniform: the chunk crosses into the next row
+              flush_row<LPR, VPL, W, kAccum>(a, row, row == head_row ? head_slot : -1, col0, acc);
+              if (!kAccum) zero_rows<LPR, VPL, W>(a, (int64_t)row + 1, ru[u], col0);
+              row = ru[u];
+#pragma unroll
+              for (int w = 0; w < VPL; ++w) acc[w] = V::zero();
+            }
+#pragma unroll
+            for (int w = 0; w < VPL; ++w) V::fma(acc[w], sv[u], b[u][w]);
+          }
+        }
+      }
+    }
+  }
+  flush_row<LPR, VPL, W, kAccum>(a, row, tail_slot >= 0 ? tail_slot : (row == head_row ? head_slot : -1), col0,
+                                 acc);
+  if (!kAccum && chunk == a.n_chunks - 1) zero_rows<LPR, VPL, W>(a, (int64_t)row + 1, a.zero_rows, col0);
+}
+
+// ------------------------------------------------------------------ fixup and fills
+
+// One warp per cut row: C[row] = (kAccum ? C[row] : 0) + sum of its partial slots, in order.
 template <int W, bool kAccum>
 __global__ void __launch_bounds__(kSpmmThreads) spmm_fixup_kernel(const SpmmArgs a) {
   using V = Vec<W>;
@@ -170,39 +324,82 @@ namespace {
 
 using KernelFn = void (*)(const SpmmArgs);
 
-template <int W, bool kAccum>
-KernelFn pick_items(int LPR, int VPL) {
+// Instantiated (lanes per row, vectors per lane) shapes. float4 path: every LPR with
+// VPL = 1, and the wider per-lane shapes that let one warp work on 2-8 rows at once (fewer
+// shuffles and row checks per nonzero). Scalar path: one warp per row.
+#define DSP_SHAPES_W4(X) \
+  X(1, 1) X(2, 1) X(4, 1) X(8, 1) X(16, 1) X(32, 1) X(4, 2) X(8, 2) X(16, 2) X(32, 2) X(2, 4) X(4, 4) X(8, 4) \
+  X(16, 4) X(32, 4) X(2, 8) X(4, 8) X(8, 8) X(16, 8) X(32, 8)
+#define DSP_SHAPES_W1(X) X(32, 1) X(32, 2) X(32, 4)
+
+bool shape_supported(int W, int LPR, int VPL) {
+#define DSP_HAS(L, P) if (LPR == L && VPL == P) return true;
   if (W == 4) {
-    if (VPL == 1) {
-      switch (LPR) {
-        case 1: return spmm_items_kernel<1, 1, W, kAccum>;
-        case 2: return spmm_items_kernel<2, 1, W, kAccum>;
-        case 4: return spmm_items_kernel<4, 1, W, kAccum>;
-        case 8: return spmm_items_kernel<8, 1, W, kAccum>;
-        case 16: return spmm_items_kernel<16, 1, W, kAccum>;
-        default: return spmm_items_kernel<32, 1, W, kAccum>;
-      }
-    }
+    DSP_SHAPES_W4(DSP_HAS)
+  } else {
+    DSP_SHAPES_W1(DSP_HAS)
   }
-  if (VPL == 1) return spmm_items_kernel<32, 1, W, kAccum>;
-  if (VPL == 2) return spmm_items_kernel<32, 2, W, kAccum>;
-  return spmm_items_kernel<32, 4, W, kAccum>;
+#undef DSP_HAS
+  return false;
+}
+
+template <int V, int W, bool kAccum>
+KernelFn kernel_for(int LPR, int VPL) {
+#define DSP_K(L, P)                                                                                   \
+  if (LPR == L && VPL == P)                                                                            \
+    return V == kRowSplit ? (KernelFn)spmm_rows_kernel<L, P, W, kAccum> : (KernelFn)spmm_nnz_kernel<L, P, W, kAccum>;
+  if (W == 4) {
+    DSP_SHAPES_W4(DSP_K)
+  } else {
+    DSP_SHAPES_W1(DSP_K)
+  }
+#undef DSP_K
+  return nullptr;
+}
+
+KernelFn select_kernel(int variant, int W, bool accum, int LPR, int VPL) {
+  if (variant == kRowSplit) {
+    if (W == 4) return accum ? kernel_for<kRowSplit, 4, true>(LPR, VPL) : kernel_for<kRowSplit, 4, false>(LPR, VPL);
+    return accum ? kernel_for<kRowSplit, 1, true>(LPR, VPL) : kernel_for<kRowSplit, 1, false>(LPR, VPL);
+  }
+  if (W == 4) return accum ? kernel_for<kNnzSplit, 4, true>(LPR, VPL) : kernel_for<kNnzSplit, 4, false>(LPR, VPL);
+  return accum ? kernel_for<kNnzSplit, 1, true>(LPR, VPL) : kernel_for<kNnzSplit, 1, false>(LPR, VPL);
 }
 
 bool aligned16(const void *p) { return ((uintptr_t)p & 15u) == 0; }
 
 }  // namespace
 
-SpmmShape spmm_shape(int N, const float *B, int64_t ldb, const float *C, int64_t ldc) {
+SpmmShape spmm_shape(int N, int variant, const float *B, int64_t ldb, const float *C, int64_t ldc) {
   SpmmShape s;
   const bool vec4 = N % 4 == 0 && ldb % 4 == 0 && ldc % 4 == 0 && aligned16(B) && aligned16(C);
   s.W = vec4 ? 4 : 1;
-  const int nv = N / s.W;  // vectors per row
-  if (vec4 && nv <= 32) {
-    int lpr = 1;
-    while (lpr < nv) lpr <<= 1;
+  const int nv = (N + s.W - 1) / s.W;  // vectors per row
+  if (vec4) {
+    // Each nonzero costs its group a few shuffles, an address and a row check no matter
+    // how many lanes share the row, so a row gets few lanes holding several float4 each
+    // (one warp then advances several rows per instruction). Measured on B200:
+    //   nnz-split: 8 vectors per lane, at most 8 lanes (N = 128 -> 4 x 8; N >= 256 -> 8 x 8
+    //              with column chunks on blockIdx.y beyond 256 columns);
+    //   row-split: 4 vectors per lane, up to 32 lanes (N = 128 -> 8 x 4).
+    static const int forced_lpr = [] {
+      const char *e = getenv("DSP_SPMM_LPR");
+      return e ? atoi(e) : 0;
+    }();
+    const int per_lane = variant == kNnzSplit ? 8 : 4;
+    const int max_lpr = variant == kNnzSplit ? 8 : 32;
+    int lpr = variant == kNnzSplit ? 2 : 1;
+    while (lpr * per_lane < nv && lpr < max_lpr) lpr <<= 1;
+    if (forced_lpr > 0) lpr = forced_lpr;
+    int vpl = 1;
+    while (lpr * vpl < nv && vpl < 8) vpl <<= 1;
+    if (!shape_supported(4, lpr, vpl)) {  // out-of-table request: one warp per row
+      lpr = nv <= 32 ? 1 : 32;
+      while (lpr < nv && lpr < 32) lpr <<= 1;
+      vpl = nv <= 32 ? 1 : nv <= 64 ? 2 : 4;
+    }
     s.LPR = lpr;
-    s.VPL = 1;
+    s.VPL = vpl;
   } else {
     s.LPR = 32;
     s.VPL = nv <= 32 ? 1 : nv <= 64 ? 2 : 4;
@@ -214,18 +411,20 @@ SpmmShape spmm_shape(int N, const float *B, int64_t ldb, const float *C, int64_t
 
 int launch_spmm(const SpmmArgs &a, bool accumulate, cudaStream_t stream) {
   if (a.N <= 0) return DSP_OK;
-  const SpmmShape s = spmm_shape(a.N, a.B, a.ldb, a.C, a.ldc);
+  const SpmmShape s = spmm_shape(a.N, a.variant, a.B, a.ldb, a.C, a.ldc);
   if (s.chunks > 65535) return fail(DSP_ERR_UNSUPPORTED, "spmm: N = %d too wide", a.N);
-  if (a.n_items > 0) {
-    KernelFn k;
-    if (s.W == 4)
-      k = accumulate ? pick_items<4, true>(s.LPR, s.VPL) : pick_items<4, false>(s.LPR, s.VPL);
-    else
-      k = accumulate ? pick_items<1, true>(s.LPR, s.VPL) : pick_items<1, false>(s.LPR, s.VPL);
+  const int64_t units = a.variant == kRowSplit ? a.n_items : a.n_chunks;
+  if (units > 0) {
+    KernelFn k = select_kernel(a.variant, s.W, accumulate, s.LPR, s.VPL);
     const int64_t groups_per_block = kSpmmThreads / s.LPR;
-    const int64_t gx = (a.n_items + groups_per_block - 1) / groups_per_block;
-    if (gx > INT32_MAX) return fail(DSP_ERR_UNSUPPORTED, "spmm: %lld items", (long long)a.n_items);
+    const int64_t gx = (units + groups_per_block - 1) / groups_per_block;
+    if (gx > INT32_MAX) return fail(DSP_ERR_UNSUPPORTED, "spmm: %lld work units", (long long)units);
     k<<<dim3((unsigned)gx, (unsigned)s.chunks), kSpmmThreads, 0, stream>>>(a);
+  } else if (!accumulate && a.zero_rows > 0) {
+    // no nonzeros at all: C = 0
+    cudaError_t e = cudaMemset2DAsync(a.C, sizeof(float) * (size_t)a.ldc, 0, sizeof(float) * (size_t)a.N,
+                                      (size_t)a.zero_rows, stream);
+    if (e != cudaSuccess) return fail(DSP_ERR_CUDA, "spmm zero fill: %s", cudaGetErrorString(e));
   }
   if (a.n_split > 0) {
     KernelFn f = s.W == 4 ? (accumulate ? spmm_fixup_kernel<4, true> : spmm_fixup_kernel<4, false>)
@@ -257,30 +456,51 @@ int launch_fill_const(float *B, int64_t n, float v, cudaStream_t stream) {
 
 int DevOperand::upload(int device_, int64_t rows_, int64_t cols_, const int64_t *row_ptr, const int32_t *row_ids,
                        int64_t m, const int64_t *indices, const float *values, int64_t first_nz, int64_t nnz_,
-                       int64_t piece_cap, bool include_empty) {
+                       int dims, bool include_empty, int variant_) {
   release();
   device = device_;
   rows = rows_;
   cols = cols_;
   nnz = nnz_;
-  ItemPlan plan;
+  zero_rows = include_empty ? rows_ : 0;
   std::vector<int64_t> rp((size_t)m + 1);
   for (int64_t i = 0; i <= m; ++i) rp[(size_t)i] = row_ptr[i] - first_nz;
-  build_items(m, row_ids, rp.data(), piece_cap, include_empty, &plan);
-  n_items = (int64_t)plan.item_out.size();
-  n_split = (int64_t)plan.split_row.size();
-  pieces = plan.pieces;
-  this->piece_cap = plan.piece_cap;
-  max_row_len = plan.max_row_len;
+  variant = variant_ >= 0 ? variant_ : choose_variant(m, rp.data(), dims);
+  std::vector<int32_t> split_row, split_ptr;
+  int rc;
+  if (variant == kRowSplit) {
+    ItemPlan plan;
+    build_items(m, row_ids, rp.data(), default_piece_cap(dims), include_empty, &plan);
+    n_items = (int64_t)plan.item_out.size();
+    pieces = plan.pieces;
+    piece_cap = plan.piece_cap;
+    max_row_len = plan.max_row_len;
+    split_row.swap(plan.split_row);
+    split_ptr.swap(plan.split_ptr);
+    if ((rc = dev_upload(&d_item_ptr, plan.item_ptr.data(), sizeof(int64_t) * plan.item_ptr.size())) ||
+        (rc = dev_upload(&d_item_out, plan.item_out.data(), sizeof(int32_t) * plan.item_out.size())))
+      return rc;
+  } else {
+    ChunkPlan plan;
+    build_chunks(m, row_ids, rp.data(), default_chunk_nnz(dims, nnz_), &plan);
+    n_chunks = plan.n_chunks;
+    chunk_nnz = plan.chunk_nnz;
+    pieces = plan.slots;
+    piece_cap = plan.chunk_nnz;
+    max_row_len = plan.max_row_len;
+    split_row.swap(plan.split_row);
+    split_ptr.swap(plan.split_ptr);
+    if ((rc = dev_upload(&d_coo_row, plan.coo_row.data(), sizeof(int32_t) * (size_t)nnz)) ||
+        (rc = dev_upload(&d_chunk_slot, plan.chunk_slot.data(), sizeof(int32_t) * (size_t)(2 * n_chunks))))
+      return rc;
+  }
+  n_split = (int64_t)split_row.size();
   std::vector<int32_t> c32((size_t)std::max<int64_t>(nnz, 1));
   parallel_for(nnz, [&](int64_t b, int64_t e) {
     for (int64_t j = b; j < e; ++j) c32[(size_t)j] = (int32_t)indices[first_nz + j];
   }, 1 << 16);
-  int rc;
-  if ((rc = dev_upload(&d_item_ptr, plan.item_ptr.data(), sizeof(int64_t) * plan.item_ptr.size())) ||
-      (rc = dev_upload(&d_item_out, plan.item_out.data(), sizeof(int32_t) * plan.item_out.size())) ||
-      (rc = dev_upload(&d_split_row, plan.split_row.data(), sizeof(int32_t) * plan.split_row.size())) ||
-      (rc = dev_upload(&d_split_ptr, plan.split_ptr.data(), sizeof(int32_t) * plan.split_ptr.size())) ||
+  if ((rc = dev_upload(&d_split_row, split_row.data(), sizeof(int32_t) * split_row.size())) ||
+      (rc = dev_upload(&d_split_ptr, split_ptr.data(), sizeof(int32_t) * split_ptr.size())) ||
       (rc = dev_upload(&d_cols, c32.data(), sizeof(int32_t) * (size_t)nnz)) ||
       (rc = dev_upload(&d_vals, values + first_nz, sizeof(float) * (size_t)nnz)))
     return rc;
@@ -288,23 +508,31 @@ int DevOperand::upload(int device_, int64_t rows_, int64_t cols_, const int64_t 
 }
 
 void DevOperand::release() {
-  for (void **p : {(void **)&d_item_ptr, (void **)&d_item_out, (void **)&d_split_row, (void **)&d_split_ptr,
-                   (void **)&d_cols, (void **)&d_vals}) {
+  for (void **p : {(void **)&d_item_ptr, (void **)&d_item_out, (void **)&d_coo_row, (void **)&d_chunk_slot,
+                   (void **)&d_split_row, (void **)&d_split_ptr, (void **)&d_cols, (void **)&d_vals}) {
     if (*p) cudaFree(*p);
     *p = nullptr;
   }
-  n_items = n_split = pieces = 0;
+  n_items = n_chunks = n_split = pieces = 0;
 }
 
 int64_t DevOperand::device_bytes() const {
-  return n_items * 12 + 8 + n_split * 8 + 4 + nnz * 8;
+  return n_items * 12 + 8 + n_chunks * 8 + (variant == kNnzSplit ? nnz * 4 : 0) + n_split * 8 + 4 + nnz * 8;
 }
 
 SpmmArgs DevOperand::args(const float *B, int64_t ldb, float *C, int64_t ldc, int N, float *partial) const {
   SpmmArgs a;
+  memset(&a, 0, sizeof a);
+  a.variant = variant;
   a.item_ptr = d_item_ptr;
   a.item_out = d_item_out;
   a.n_items = n_items;
+  a.coo_row = d_coo_row;
+  a.chunk_slot = d_chunk_slot;
+  a.n_chunks = n_chunks;
+  a.chunk_nnz = chunk_nnz;
+  a.nnz = nnz;
+  a.zero_rows = zero_rows;
   a.split_row = d_split_row;
   a.split_ptr = d_split_ptr;
   a.n_split = n_split;
@@ -335,16 +563,14 @@ void prefer_l1_carveout() {
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 31 && (done_mask >> dev) & 1) return;
-  const KernelFn ks[] = {
-      pick_items<4, false>(1, 1),  pick_items<4, false>(2, 1),  pick_items<4, false>(4, 1),
-      pick_items<4, false>(8, 1),  pick_items<4, false>(16, 1), pick_items<4, false>(32, 1),
-      pick_items<4, false>(32, 2), pick_items<4, false>(32, 4), pick_items<4, true>(1, 1),
-      pick_items<4, true>(2, 1),   pick_items<4, true>(4, 1),   pick_items<4, true>(8, 1),
-      pick_items<4, true>(16, 1),  pick_items<4, true>(32, 1),  pick_items<4, true>(32, 2),
-      pick_items<4, true>(32, 4),  pick_items<1, false>(32, 1), pick_items<1, false>(32, 2),
-      pick_items<1, false>(32, 4), pick_items<1, true>(32, 1),  pick_items<1, true>(32, 2),
-      pick_items<1, true>(32, 4)};
-  for (KernelFn k : ks) cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout, 0);
+  for (int v = 0; v < 2; ++v)
+    for (int w : {4, 1})
+      for (int acc = 0; acc < 2; ++acc)
+        for (int lpr = 1; lpr <= 32; lpr <<= 1)
+          for (int vpl = 1; vpl <= 8; vpl <<= 1)
+            if (shape_supported(w, lpr, vpl))
+              cudaFuncSetAttribute(select_kernel(v, w, acc != 0, lpr, vpl),
+                                   cudaFuncAttributePreferredSharedMemoryCarveout, 0);
   cudaGetLastError();
   if (dev < 31) done_mask |= 1 << dev;
 }
@@ -370,7 +596,7 @@ extern "C" int dsp_device_count(void) {
   return n;
 }
 
-extern "C" int dsp_spmm_plan_create(int device, const dsp_csr *a, int dims_hint, dsp_spmm_plan **out) {
+extern "C" int dsp_spmm_plan_create(int device, const dsp_csr *a, int dims_hint, int variant, dsp_spmm_plan **out) {
   DSP_TRY_ARG(a && out && a->indptr, "dsp_spmm_plan_create: null argument");
   DSP_TRY_ARG(a->num_cols <= INT32_MAX && a->num_rows <= INT32_MAX, "dsp_spmm_plan_create: matrix too large for int32 ids");
   *out = nullptr;
@@ -378,10 +604,12 @@ extern "C" int dsp_spmm_plan_create(int device, const dsp_csr *a, int dims_hint,
   if (e != cudaSuccess) return fail(DSP_ERR_CUDA, "cudaSetDevice(%d): %s", device, cudaGetErrorString(e));
   prefer_l1_carveout();
   dsp_spmm_plan *p = new dsp_spmm_plan();
+  const int dims = dims_hint > 0 ? dims_hint : 128;
+  DSP_TRY_ARG(variant >= -1 && variant <= 1, "dsp_spmm_plan_create: variant %d", variant);
   int rc = p->op.upload(device, a->num_rows, a->num_cols, a->indptr, nullptr, a->num_rows, a->indices, a->values, 0,
-                        a->nnz, default_piece_cap(dims_hint > 0 ? dims_hint : 128), true);
+                        a->nnz, dims, true, variant);
   if (rc == DSP_OK && p->op.pieces > 0) {
-    p->scratch_floats = p->op.pieces * (int64_t)std::max(dims_hint, 1);
+    p->scratch_floats = p->op.pieces * (int64_t)dims;
     e = cudaMalloc(&p->scratch, sizeof(float) * (size_t)p->scratch_floats);
     if (e != cudaSuccess) rc = fail(DSP_ERR_NOMEM, "spmm scratch: %s", cudaGetErrorString(e));
   }
@@ -406,7 +634,8 @@ extern "C" int dsp_spmm_plan_info(const dsp_spmm_plan *p, dsp_spmm_info *info) {
   info->rows = p->op.rows;
   info->cols = p->op.cols;
   info->nnz = p->op.nnz;
-  info->items = p->op.n_items;
+  info->variant = p->op.variant;
+  info->items = p->op.variant == kRowSplit ? p->op.n_items : p->op.n_chunks;
   info->split_rows = p->op.n_split;
   info->pieces = p->op.pieces;
   info->piece_cap = p->op.piece_cap;

@@ -16,14 +16,16 @@ from .matrix import Csr
 
 
 class SpmmPlan:
-    def __init__(self, a: Csr, device: int = 0, dims_hint: int = 128):
+    VARIANTS = {None: -1, "auto": -1, "rows": 0, "nnz": 1}
+
+    def __init__(self, a: Csr, device: int = 0, dims_hint: int = 128, variant: str | None = None):
         self.device = device
         self.rows = a.num_rows
         self.cols = a.num_cols
         self.nnz = a.nnz
         c = a.to_c()
         h = c_vp()
-        call("dsp_spmm_plan_create", device, ctypes.byref(c), dims_hint, ctypes.byref(h))
+        call("dsp_spmm_plan_create", device, ctypes.byref(c), dims_hint, self.VARIANTS[variant], ctypes.byref(h))
         self._h = h
 
     def info(self) -> dict:

@@ -191,27 +191,34 @@ int dsp_traffic_inter(int me, int ranks_per_node, int num_nodes, int T, const in
 double dsp_gflops(int64_t nnz, int dims, double avg_ms);
 
 /* ---------------------------------------------------------------- single-GPU SpMM */
-/* A device-resident CSR operand prepared for the sm_100a SpMM kernels: the rows are cut
- * into work items (whole rows, heavy rows split into bounded pieces whose partial sums
- * are combined in a fixed order), column ids stored as int32. Replaces the per-tile
+/* A device-resident CSR operand prepared for the sm_100a SpMM kernels, column ids stored
+ * as int32, cut into work units by one of two decompositions chosen from the row-length
+ * statistics: row-split (one item per row, heavy rows cut into bounded pieces) or
+ * nnz-split (equal chunks of consecutive nonzeros across row boundaries, with a row id
+ * per nonzero). Partial rows are combined in a fixed order. Replaces the per-tile
  * cusparseCreateCoo + cusparseSpMM(ALG_DEFAULT) of src/dist_spmm_node.cu:233-234 and
  * :354-385. */
 typedef struct dsp_spmm_plan dsp_spmm_plan;
 
 typedef struct dsp_spmm_info {
   int64_t rows, cols, nnz;
-  int64_t items;       /* work items (rows or row pieces)              */
-  int64_t split_rows;  /* rows cut into pieces                          */
-  int64_t pieces;      /* pieces of split rows (scratch slots)          */
-  int64_t piece_cap;   /* maximum nonzeros per piece                    */
+  int64_t variant;     /* 0 = row-split items, 1 = nnz-split chunks     */
+  int64_t items;       /* work units (row items or nonzero chunks)      */
+  int64_t split_rows;  /* rows cut across work units                    */
+  int64_t pieces;      /* partial-row scratch slots                     */
+  int64_t piece_cap;   /* maximum nonzeros per unit                     */
   int64_t max_row_len; /* longest row                                   */
   int64_t scratch_bytes;
   int64_t device_bytes; /* all device memory the plan holds             */
 } dsp_spmm_info;
 
 /* Build the plan on `device` from a host CSR (indices < 2^31 required). dims_hint is the
- * dense width the plan is tuned for (it only sets the piece length). */
-int dsp_spmm_plan_create(int device, const dsp_csr *a, int dims_hint, dsp_spmm_plan **out);
+ * dense width the plan is tuned for (it sets the piece / chunk length); variant: -1 picks
+ * from the row-length statistics, 0 forces row-split, 1 forces nnz-split. */
+#define DSP_VARIANT_AUTO -1
+#define DSP_VARIANT_ROWS 0
+#define DSP_VARIANT_NNZ 1
+int dsp_spmm_plan_create(int device, const dsp_csr *a, int dims_hint, int variant, dsp_spmm_plan **out);
 void dsp_spmm_plan_destroy(dsp_spmm_plan *p);
 int dsp_spmm_plan_info(const dsp_spmm_plan *p, dsp_spmm_info *info);
 

@@ -1,4 +1,5 @@
-"""Parity of the sm_100a SpMM kernels (through the C ABI) with the CPU oracle.
+"""Parity of the sm_100a SpMM kernels (through the C ABI) with the CPU oracle, for both
+work decompositions (row-split and nnz-split) and the automatic choice.
 
 Tolerance (fp32, from the engine's specification): elementwise
     |C_gpu - C_ref| <= 1e-5 * (|A|.|B|)
@@ -12,13 +13,14 @@ import oracle
 
 pytestmark = pytest.mark.gpu
 RTOL = 1e-5
+VARIANTS = ["rows", "nnz"]
 
 
-def _run(A, N, seed=3, accumulate=False, C0=None, dims_hint=None):
+def _run(A, N, seed=3, accumulate=False, C0=None, dims_hint=None, variant=None):
     import torch
     from distspmm_b200.spmm import SpmmPlan
     B = d.dense_b(A.num_cols, N, seed)
-    plan = SpmmPlan(A, 0, dims_hint or N)
+    plan = SpmmPlan(A, 0, dims_hint or N, variant)
     Bt = torch.from_numpy(B).cuda()
     Ct = torch.from_numpy(C0).cuda() if C0 is not None else None
     C = plan(Bt, Ct, accumulate=accumulate)
@@ -42,49 +44,64 @@ def rmat13():
     return d.gen_rmat(13, seed=2)
 
 
+@pytest.mark.parametrize("variant", VARIANTS)
 @pytest.mark.parametrize("N", [1, 3, 4, 8, 16, 32, 64, 96, 100, 128, 256, 384, 512, 640])
-def test_rmat_widths(gpu, rmat13, N):
-    B, C, plan = _run(rmat13, N)
+def test_rmat_widths(gpu, rmat13, N, variant):
+    B, C, plan = _run(rmat13, N, variant=variant)
     info = plan.info()
-    # pieces hold at most ~32K multiply-adds: the hub rows (max degree ~2.2K) are split
-    # from N = 16 up
-    assert (info["pieces"] > 0) == (info["max_row_len"] > info["piece_cap"])
-    if N >= 16:
-        assert info["pieces"] > 0
+    assert info["variant"] == VARIANTS.index(variant)
+    if variant == "rows":
+        # pieces hold at most ~32K multiply-adds: the hub rows (max degree ~2.2K) are split
+        # from N = 16 up
+        assert (info["pieces"] > 0) == (info["max_row_len"] > info["piece_cap"])
+        if N >= 16:
+            assert info["pieces"] > 0
+    else:
+        assert info["items"] == -(-rmat13.nnz // info["piece_cap"])  # chunks of equal nonzeros
     _check(rmat13, B, C)
 
 
+@pytest.mark.parametrize("variant", VARIANTS + [None])
 @pytest.mark.parametrize("kind,kw,N", [
     ("rmat", dict(scale=15), 32),   # configuration 1 of the benchmark set
     ("stencil27", dict(n=24), 128),
     ("uniform", dict(rows=1 << 14, nnz_per_row=32), 256),
 ])
-def test_matrix_families(gpu, kind, kw, N):
+def test_matrix_families(gpu, kind, kw, N, variant):
     A = d.make_matrix(kind, seed=4, **kw)
-    B, C, _ = _run(A, N)
+    B, C, _ = _run(A, N, variant=variant)
     _check(A, B, C)
 
 
-def test_accumulate(gpu, rmat13):
+def test_variant_choice_follows_row_statistics(gpu):
+    from distspmm_b200.spmm import SpmmPlan
+    assert SpmmPlan(d.gen_rmat(12, seed=1), 0, 128).info()["variant"] == 1      # skewed, many empty rows
+    assert SpmmPlan(d.gen_stencil27(12, seed=1), 0, 128).info()["variant"] == 0  # regular rows
+
+
+@pytest.mark.parametrize("variant", VARIANTS)
+def test_accumulate(gpu, rmat13, variant):
     C0 = d.dense_b(rmat13.num_rows, 128, seed=77)
-    B, C, _ = _run(rmat13, 128, accumulate=True, C0=C0.copy())
+    B, C, _ = _run(rmat13, 128, accumulate=True, C0=C0.copy(), variant=variant)
     _check(rmat13, B, C, C0)
 
 
-def test_deterministic(gpu, rmat13):
-    _, C1, _ = _run(rmat13, 128)
-    _, C2, _ = _run(rmat13, 128)
+@pytest.mark.parametrize("variant", VARIANTS)
+def test_deterministic(gpu, rmat13, variant):
+    _, C1, _ = _run(rmat13, 128, variant=variant)
+    _, C2, _ = _run(rmat13, 128, variant=variant)
     assert np.array_equal(C1, C2)  # fixed summation order, no atomics
 
 
-def test_strided_and_unaligned_operands(gpu, rmat13):
+@pytest.mark.parametrize("variant", VARIANTS)
+def test_strided_and_unaligned_operands(gpu, rmat13, variant):
     """B and C as column windows of wider buffers (ld > N, not 16-byte aligned: the
     scalar kernel path)."""
     import torch
     from distspmm_b200.spmm import SpmmPlan
     N = 64
     Bw = d.dense_b(rmat13.num_cols, N + 3, seed=5)
-    plan = SpmmPlan(rmat13, 0, N)
+    plan = SpmmPlan(rmat13, 0, N, variant)
     Bt = torch.from_numpy(Bw).cuda()
     Cw = torch.full((rmat13.num_rows, N + 5), 7.0, device="cuda")
     plan(Bt[:, 1:N + 1], Cw[:, 2:N + 2])
@@ -94,26 +111,51 @@ def test_strided_and_unaligned_operands(gpu, rmat13):
     _check(rmat13, np.ascontiguousarray(Bw[:, 1:N + 1]), C[:, 2:N + 2])
 
 
-def test_edge_cases(gpu):
+@pytest.mark.parametrize("variant", VARIANTS)
+def test_edge_cases(gpu, variant):
     import torch
     from distspmm_b200.spmm import SpmmPlan
-    # all rows empty
+    # all rows empty (C must still be written: poison it first)
     E = d.Csr(np.zeros(11, np.int64), np.zeros(0, np.int64), np.zeros(0, np.float32), 10, 10)
-    B, C, _ = _run(E, 32)
-    assert (C == 0).all()
-    # one huge row (forces many pieces) among empty rows, and a single-row matrix
+    plan = SpmmPlan(E, 0, 32, variant)
+    C = torch.full((10, 32), float("nan"), device="cuda")
+    plan(torch.ones((10, 32), device="cuda"), C)
+    assert (C.cpu().numpy() == 0).all()
+    # one huge row (forces many pieces / chunks) among empty rows, and a single-row matrix
     n = 200_000
     idx = np.arange(n, dtype=np.int64)
     H = d.Csr(np.array([0, 0, n, n], np.int64), idx, np.random.default_rng(1).random(n).astype(np.float32), 3, n)
-    B, C, plan = _run(H, 128)
+    B, C, plan = _run(H, 128, variant=variant)
     assert plan.info()["pieces"] >= n // plan.info()["piece_cap"]
     _check(H, B, C)
     R = d.Csr(np.array([0, 3], np.int64), np.array([0, 1, 2], np.int64), np.ones(3, np.float32), 1, 3)
-    B, C, _ = _run(R, 5)
+    B, C, _ = _run(R, 5, variant=variant)
     _check(R, B, C)
+    # empty rows at both ends and between rows of a chunk; one nonzero per row
+    G = d.Csr(np.array([0, 0, 0, 1, 1, 2, 3, 3, 3], np.int64), np.array([4, 0, 7], np.int64),
+              np.array([2.0, 3.0, 5.0], np.float32), 8, 8)
+    plan = SpmmPlan(G, 0, 16, variant)
+    Bg = d.dense_b(8, 16, seed=1)
+    C = torch.full((8, 16), float("nan"), device="cuda")
+    plan(torch.from_numpy(Bg).cuda(), C)
+    torch.cuda.synchronize()
+    _check(G, Bg, C.cpu().numpy())
     # zero-width B
-    plan = SpmmPlan(R, 0, 4)
+    plan = SpmmPlan(R, 0, 4, variant)
     plan(torch.zeros((3, 0), device="cuda"))
+
+
+def test_nonaccumulating_launch_overwrites_every_row(gpu, rmat13):
+    """C starts as NaN; every row, empty ones included, must be written."""
+    import torch
+    from distspmm_b200.spmm import SpmmPlan
+    for variant in VARIANTS:
+        plan = SpmmPlan(rmat13, 0, 128, variant)
+        B = d.dense_b(rmat13.num_cols, 128, seed=3)
+        C = torch.full((rmat13.num_rows, 128), float("nan"), device="cuda")
+        plan(torch.from_numpy(B).cuda(), C)
+        torch.cuda.synchronize()
+        _check(rmat13, B, C.cpu().numpy())
 
 
 def test_reference_run_mode_b_all_ones(gpu):
