@@ -26,6 +26,8 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <mutex>
+
 #include "device.cuh"
 #include "internal.h"
 
@@ -667,4 +669,251 @@ extern "C" int dsp_spmm_f32(dsp_spmm_plan *p, const float *B, int64_t ldb, float
   }
   SpmmArgs a = p->op.args(B, ldb, C, ldc, N, p->scratch);
   return launch_spmm(a, accumulate != 0, (cudaStream_t)stream);
+}
+
+// ------------------------------------------------------------------ allocation-free entry point
+//
+// dsp_spmm_csr_f32_noalloc: C (+)= A.B for a CSR matrix the caller already holds in device
+// memory (int64 indptr / indices, fp32 values: the reference's on-disk and SparseMatrix
+// layout), without allocating any device memory. It is meant for callers that cannot or
+// must not call cudaMalloc: code running on a latency-critical stream next to other work
+// (cudaMalloc / cudaFree can synchronise the whole device), frameworks that own all device
+// memory through their own pool and forbid allocations behind their back, and steps that
+// must not fail halfway with an out-of-memory error.
+//
+// It is the nnz-split kernel without host planning: every chunk of chunk_nnz nonzeros finds
+// its first row by binary search in indptr; a row cut by chunk boundaries leaves one partial
+// row per chunk it touches, in slot 2c ("cut before", the chunk's first row) or 2c + 1 ("cut
+// after only", the chunk's last row), and the chunk where the row ends sums those slots in
+// chunk order (deterministic). The slots are the only scratch and live in the static array
+// below: kNoAllocScratchBytes on every GPU that loads this library, held until exit.
+// Nothing in it has to start at zero (every slot read was written by the same call), but
+// all calls on a device share it, so calls that overlap on the GPU (different streams)
+// race on it.
+
+namespace dsp {
+
+constexpr size_t kNoAllocScratchBytes = size_t(32) << 20;
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchBytes / sizeof(float)];
+
+struct CsrChunkArgs {
+  SpmmArgs base;           // B, C, N, ldb, ldc; base.partial = the slots
+  const int64_t *indptr;   // [rows + 1]
+  const int64_t *indices;  // [nnz]
+  int64_t rows;
+};
+
+// Last row r with indptr[r] <= p (the nonempty row holding nonzero p, 0 <= p < nnz).
+__device__ __forceinline__ int64_t row_holding(const int64_t *indptr, int64_t rows, int64_t p) {
+  int64_t lo = 0, hi = rows;  // indptr[lo] <= p < indptr[hi]
+  while (hi - lo > 1) {
+    const int64_t mid = (lo + hi) >> 1;
+    if (__ldg(indptr + mid) <= p) lo = mid;
+    else hi = mid;
+  }
+  return lo;
+}
+
+template <int LPR, int VPL, int W, bool kAccum>
+__global__ void __launch_bounds__(kSpmmThreads) spmm_csr_chunks_kernel(const CsrChunkArgs ca) {
+  using V = Vec<W>;
+  using T = typename V::T;
+  const SpmmArgs &a = ca.base;
+  constexpr int U = loads_in_flight<LPR, VPL>();
+  constexpr int K = entries_per_lane<LPR>();
+  const int lane = threadIdx.x & (LPR - 1);
+  const int64_t chunk = ((int64_t)blockIdx.x * kSpmmThreads + threadIdx.x) / LPR;
+  if (chunk >= a.n_chunks) return;
+  const unsigned gmask = group_mask<LPR>();
+  const int col0 = blockIdx.y * (LPR * VPL * W) + lane * W;
+  const int64_t s = chunk * a.chunk_nnz, e = min(s + a.chunk_nnz, a.nnz);
+  const uint64_t pol = evict_last_policy();
+
+  int64_t row = row_holding(ca.indptr, ca.rows, s);
+  int64_t rbeg = __ldg(ca.indptr + row), rend = __ldg(ca.indptr + row + 1);
+  if (!kAccum) zero_rows<LPR, VPL, W>(a, s > 0 ? row_holding(ca.indptr, ca.rows, s - 1) + 1 : 0, row, col0);
+  // partial slot of the current row: cut before this chunk -> 2c, cut only after -> 2c + 1
+  auto slot_of = [&](int64_t b, int64_t en) -> int32_t {
+    return b < s ? (int32_t)(2 * chunk) : (en > e ? (int32_t)(2 * chunk + 1) : -1);
+  };
+
+  T acc[VPL];
+#pragma unroll
+  for (int w = 0; w < VPL; ++w) acc[w] = V::zero();
+
+  for (int64_t base = s; base < e; base += LPR * K) {
+    int64_t c[K];
+    float v[K];
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      const int64_t p = base + k * LPR + lane;
+      c[k] = p < e ? (int64_t)__ldcs((const long long *)ca.indices + p) : 0;
+      v[k] = p < e ? __ldcs(a.vals + p) : 0.f;
+    }
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      const int64_t kb = base + k * LPR;
+      if (kb >= e) break;
+      const int n = (int)min((int64_t)LPR, e - kb);
+      for (int j = 0; j < n; j += U) {
+        T b[U][VPL];
+        float sv[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int64_t cj = __shfl_sync(gmask, (long long)c[k], j + u, LPR);
+          sv[u] = __shfl_sync(gmask, v[k], j + u, LPR);
+          const float *brow = a.B + cj * a.ldb;
+#pragma unroll
+          for (int w = 0; w < VPL; ++w) {
+            const int col = col0 + w * LPR * W;
+            b[u][w] = (j + u < n && col < a.N) ? V::ldg(brow + col, pol) : V::zero();
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int64_t p = kb + j + u;
+          if (j + u < n) {
+            if (p >= rend) {  // group-uniform: the chunk crosses into a later row
+              flush_row<LPR, VPL, W, kAccum>(a, (int32_t)row, slot_of(rbeg, rend), col0, acc);
+              const int64_t next = row_holding(ca.indptr, ca.rows, p);
+              if (!kAccum) zero_rows<LPR, VPL, W>(a, row + 1, next, col0);
+              row = next;
+              rbeg = __ldg(ca.indptr + row);
+              rend = __ldg(ca.indptr + row + 1);
+#pragma unroll
+              for (int w = 0; w < VPL; ++w) acc[w] = V::zero();
+            }
+#pragma unroll
+            for (int w = 0; w < VPL; ++w) V::fma(acc[w], sv[u], b[u][w]);
+          }
+        }
+      }
+    }
+  }
+  flush_row<LPR, VPL, W, kAccum>(a, (int32_t)row, slot_of(rbeg, rend), col0, acc);
+  if (!kAccum && chunk == a.n_chunks - 1) zero_rows<LPR, VPL, W>(a, row + 1, ca.rows, col0);
+}
+
+// One warp per chunk: if the chunk's first row began in an earlier chunk c0 and ends here,
+// C[row] = (kAccum ? C[row] : 0) + slot[2 c0 + 1] + slot[2k] for k = c0+1 .. this chunk.
+template <int W, bool kAccum>
+__global__ void __launch_bounds__(kSpmmThreads) spmm_csr_chunks_fixup_kernel(const CsrChunkArgs ca) {
+  using V = Vec<W>;
+  using T = typename V::T;
+  const SpmmArgs &a = ca.base;
+  const int lane = threadIdx.x & 31;
+  const int64_t chunk = ((int64_t)blockIdx.x * kSpmmThreads + threadIdx.x) >> 5;
+  if (chunk >= a.n_chunks) return;
+  const int64_t s = chunk * a.chunk_nnz, e = min(s + a.chunk_nnz, a.nnz);
+  const int64_t row = row_holding(ca.indptr, ca.rows, s);
+  const int64_t rbeg = __ldg(ca.indptr + row), rend = __ldg(ca.indptr + row + 1);
+  if (!(rbeg < s && rend <= e)) return;  // not a cut row that ends in this chunk
+  const int64_t c0 = rbeg / a.chunk_nnz;
+  float *dst = a.C + row * a.ldc;
+  for (int col = lane * W; col < a.N; col += 32 * W) {
+    T r = kAccum ? V::ld(dst + col) : V::zero();
+    V::add(r, V::ld(a.partial + (2 * c0 + 1) * (int64_t)a.N + col));
+    for (int64_t k = c0 + 1; k <= chunk; ++k) V::add(r, V::ld(a.partial + (2 * k) * (int64_t)a.N + col));
+    V::st(dst + col, r);
+  }
+}
+
+namespace {
+
+using CsrKernelFn = void (*)(const CsrChunkArgs);
+
+// Every shape spmm_shape() can return.
+template <int W, bool kAccum>
+CsrKernelFn csr_kernel_for(int LPR, int VPL) {
+#define DSP_CK(L, P) \
+  if (LPR == L && VPL == P) return spmm_csr_chunks_kernel<L, P, W, kAccum>;
+  if (W == 4) {
+    DSP_SHAPES_W4(DSP_CK)
+  } else {
+    DSP_SHAPES_W1(DSP_CK)
+  }
+#undef DSP_CK
+  return nullptr;
+}
+
+std::mutex g_noalloc_mu;
+float *g_noalloc_ptr[64] = {};
+
+// Device address of this device's static scratch (looked up once per device, with that
+// device current).
+int noalloc_scratch(int dev, float **out) {
+  if (dev < 0 || dev >= 64) return fail(DSP_ERR_UNSUPPORTED, "device ordinal %d", dev);
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void *p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return fail(DSP_ERR_CUDA, "cudaGetSymbolAddress(scratch): %s", cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = (float *)p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return DSP_OK;
+}
+
+}  // namespace
+}  // namespace dsp
+
+extern "C" int dsp_spmm_csr_f32_noalloc(const int64_t *indptr, const int64_t *indices, const float *values,
+                                        int64_t rows, int64_t cols, int64_t nnz, const float *B, int64_t ldb,
+                                        float *C, int64_t ldc, int N, int accumulate, void *stream) {
+  DSP_TRY_ARG(rows >= 0 && cols >= 0 && nnz >= 0, "dsp_spmm_csr_f32_noalloc: negative size");
+  DSP_TRY_ARG(N >= 0 && ldb >= N && ldc >= N, "dsp_spmm_csr_f32_noalloc: N=%d ldb=%lld ldc=%lld", N,
+              (long long)ldb, (long long)ldc);
+  if (N > DSP_NOALLOC_MAX_N)
+    return fail(DSP_ERR_UNSUPPORTED, "dsp_spmm_csr_f32_noalloc: N = %d exceeds the maximum %d of its %zu-byte scratch",
+                N, DSP_NOALLOC_MAX_N, kNoAllocScratchBytes);
+  if (rows > INT32_MAX)
+    return fail(DSP_ERR_UNSUPPORTED, "dsp_spmm_csr_f32_noalloc: %lld rows exceed 2^31 - 1", (long long)rows);
+  if (N == 0 || rows == 0) return DSP_OK;
+  DSP_TRY_ARG(indptr && C && (nnz == 0 || (indices && values && B)), "dsp_spmm_csr_f32_noalloc: null argument");
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(DSP_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  float *slots = nullptr;
+  int rc = noalloc_scratch(dev, &slots);
+  if (rc) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (nnz == 0) {
+    if (accumulate) return DSP_OK;
+    e = cudaMemset2DAsync(C, sizeof(float) * (size_t)ldc, 0, sizeof(float) * (size_t)N, (size_t)rows, st);
+    return e == cudaSuccess ? DSP_OK : fail(DSP_ERR_CUDA, "zero fill: %s", cudaGetErrorString(e));
+  }
+  // chunk length: the usual one, grown until two slots per chunk fit the static scratch
+  const int64_t max_chunks = (int64_t)(kNoAllocScratchBytes / sizeof(float)) / (2 * (int64_t)N);
+  int64_t chunk = default_chunk_nnz(N, nnz);
+  if ((nnz + chunk - 1) / chunk > max_chunks) chunk = ((nnz + max_chunks - 1) / max_chunks + 31) & ~int64_t(31);
+  CsrChunkArgs ca;
+  memset(&ca, 0, sizeof ca);
+  ca.base.vals = values;
+  ca.base.B = B;
+  ca.base.ldb = ldb;
+  ca.base.C = C;
+  ca.base.ldc = ldc;
+  ca.base.partial = slots;
+  ca.base.N = N;
+  ca.base.nnz = nnz;
+  ca.base.chunk_nnz = chunk;
+  ca.base.n_chunks = (nnz + chunk - 1) / chunk;
+  ca.indptr = indptr;
+  ca.indices = indices;
+  ca.rows = rows;
+  const SpmmShape s = spmm_shape(N, kNnzSplit, B, ldb, C, ldc);
+  CsrKernelFn k = nullptr;
+  if (s.W == 4)
+    k = accumulate ? csr_kernel_for<4, true>(s.LPR, s.VPL) : csr_kernel_for<4, false>(s.LPR, s.VPL);
+  else
+    k = accumulate ? csr_kernel_for<1, true>(s.LPR, s.VPL) : csr_kernel_for<1, false>(s.LPR, s.VPL);
+  if (!k) return fail(DSP_ERR_UNSUPPORTED, "dsp_spmm_csr_f32_noalloc: no kernel for N = %d", N);
+  const int64_t groups_per_block = kSpmmThreads / s.LPR;
+  const int64_t gx = (ca.base.n_chunks + groups_per_block - 1) / groups_per_block;
+  k<<<dim3((unsigned)gx, (unsigned)s.chunks), kSpmmThreads, 0, st>>>(ca);
+  CsrKernelFn f = s.W == 4 ? (accumulate ? spmm_csr_chunks_fixup_kernel<4, true> : spmm_csr_chunks_fixup_kernel<4, false>)
+                           : (accumulate ? spmm_csr_chunks_fixup_kernel<1, true> : spmm_csr_chunks_fixup_kernel<1, false>);
+  f<<<(unsigned)((ca.base.n_chunks * 32 + kSpmmThreads - 1) / kSpmmThreads), kSpmmThreads, 0, st>>>(ca);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? DSP_OK : fail(DSP_ERR_CUDA, "dsp_spmm_csr_f32_noalloc launch: %s", cudaGetErrorString(e));
 }

@@ -228,6 +228,26 @@ int dsp_spmm_plan_info(const dsp_spmm_plan *p, dsp_spmm_info *info);
 int dsp_spmm_f32(dsp_spmm_plan *p, const float *B, int64_t ldb, float *C, int64_t ldc, int N,
                  int accumulate, void *stream);
 
+/* Allocation-free SpMM (no counterpart in the reference). C = A*B (accumulate = 0) or
+ * C += A*B on the current CUDA device, for a CSR matrix the caller already holds in device
+ * memory in the reference's layout (int64 indptr[rows+1], int64 indices[nnz], fp32
+ * values[nnz]); B (cols x N, ldb) and C (rows x N, ldc) as for dsp_spmm_f32.
+ * For callers that cannot call cudaMalloc: code on a latency-critical stream beside other
+ * work (cudaMalloc / cudaFree may synchronise the device), frameworks whose own memory pool
+ * owns the device and forbids allocations behind its back, and steps that must not fail
+ * with out-of-memory midway. It allocates no device memory and calls no allocating
+ * routine: its only scratch (partial rows of rows cut between work chunks) is a static
+ * 32 MiB device array that every GPU loading the library holds until exit.
+ * Limits: N <= DSP_NOALLOC_MAX_N and rows < 2^31 (DSP_ERR_UNSUPPORTED otherwise).
+ * The first call on a device looks up that device's scratch address
+ * (cudaGetSymbolAddress), so make it before any stream capture. All calls on a device share
+ * the scratch: calls that overlap on the GPU (e.g. on two streams) race; serialise them.
+ * The scratch keeps the last call's contents; no call relies on it being zero. */
+#define DSP_NOALLOC_MAX_N 2048
+int dsp_spmm_csr_f32_noalloc(const int64_t *indptr, const int64_t *indices, const float *values,
+                             int64_t rows, int64_t cols, int64_t nnz, const float *B, int64_t ldb,
+                             float *C, int64_t ldc, int N, int accumulate, void *stream);
+
 /* ---------------------------------------------------------------- distributed rank */
 /* One GPU's share of the distributed SpMM: the local rows of A cut into segments by the
  * owner of each column tile (own tiles first, then peers in ring order (me+k)%P as in
