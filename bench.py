@@ -106,6 +106,15 @@ def config_of(a, world, nnz, M):
             "b": "U(-1,1) fp32 row-major"}
 
 
+def host_threads():
+    """All host threads this process may run on (torchrun sets OMP_NUM_THREADS=1; the CPU
+    arms pass the thread count explicitly)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 def measured_peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -172,7 +181,7 @@ def cpu_spmm_baseline(A, B, budget_s=10.0, max_reps=5):
     import numpy as np
 
     import oracle
-    threads = oracle.max_threads()
+    threads = host_threads()
     C = np.empty((A.num_rows, B.shape[1]), np.float32)
     t0 = time.perf_counter()
     oracle.spmm_f32(A.indptr, A.indices, A.values, B, threads=threads, out=C)
@@ -209,7 +218,7 @@ def run_reference(a, rank, world):
     import numpy as np
 
     import oracle
-    threads = oracle.max_threads()
+    threads = host_threads()
     C = np.empty((A.num_rows, a.dims), np.float32)
     t0 = time.perf_counter()
     oracle.spmm_f32(A.indptr, A.indices, A.values, B, threads=threads, out=C)
@@ -260,6 +269,7 @@ def main(argv=None):
     comm = None
     if world > 1:
         import torch.distributed as dist
+        os.environ.setdefault("NCCL_DEBUG", "WARN")  # keep rank 0's stdout to the one JSON line
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
         comm = TorchComm()
 
@@ -313,12 +323,17 @@ def main(argv=None):
         e1.synchronize()
         step_ms.append(e0.elapsed_time(e1))
         compute_ms.append(R.last_compute_ms())
+        timeline = R.timeline()
     torch.cuda.synchronize(dev)
     if comm is not None:
         comm.barrier()
     wall = time.perf_counter() - t_wall
     clk = clocks.stop() if clocks else None
 
+    # compute-stream time spent waiting for fetches in the last step (segments not back to back)
+    segs = [(t[2], t[3]) for t in timeline if t[2] is not None]
+    idle = (segs[-1][1] - segs[0][0]) - sum(e - b for b, e in segs) if segs else 0.0
+    idle_max = comm.allreduce_max(idle) if comm is not None else idle
     mean_step = statistics.mean(step_ms)
     mean_compute = statistics.mean(compute_ms)
     if comm is not None:
@@ -396,7 +411,9 @@ def main(argv=None):
         "e2e": e2e, "cpu_baseline": cpu, "clocks": clk,
         "gpu_launches": a.steps * st["kernels_per_step"],
         "nvlink": {"fetched_bytes_per_step": fetch_bytes,
-                   "max_rank_compute_ms": round(t_comp_max, 4)},
+                   "max_rank_compute_ms": round(t_comp_max, 4),
+                   "max_rank_compute_idle_ms": round(idle_max, 4),
+                   "timeline_rank0": timeline if rank == 0 else None},
         "wall_s_timed_region": round(wall, 3),
     }
     if rank == 0:

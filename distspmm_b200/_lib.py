@@ -129,6 +129,7 @@ PROTOTYPES = {
     "dsp_rank_step": (c_int, [c_vp, c_vp]),
     "dsp_rank_download_c": (c_int, [c_vp, c_vp, c_vp]),
     "dsp_rank_last_compute_ms": (c_int, [c_vp, P(c_f32)]),
+    "dsp_rank_last_timeline": (c_int, [c_vp, P(c_f32), c_int]),
     "dsp_run": (c_int, [P(dsp_args), P(dsp_report)]),
 }
 

@@ -7,20 +7,24 @@
 //         recycled (the reference's 4-slot ring of src/dist_spmm_node.cu:199-203 with its
 //         reuse race, replaced by one full-height buffer: 180 GB HBM holds B at every
 //         configuration this engine targets).
-//   C     [m_local x dims] fp32 row-major.
-//   A     one DevOperand per segment: segment k holds the local nonzeros whose column
-//         tile is owned by rank (me + k) % P (the reference's visit order,
-//         src/dist_spmm_node.cu:339-343). Segment 0 lists every local row (it writes C);
-//         later segments list only rows with nonzeros there (they accumulate).
-//   scratch: partial rows of heavy-row pieces, shared by the segments (they run in order
-//         on one stream).
+//   C     [m_local x dims] fp32 row-major, every row written exactly once per step.
+//   A     one DevOperand per phase. Peers are visited in the reference's ring order
+//         (me + k) % P (src/dist_spmm_node.cu:339-343); a local row belongs to phase k, the
+//         latest ring position among the owners of its columns, and phase k holds whole
+//         rows (all their nonzeros). Phase 0 = rows that need only tiles this rank owns.
+//         Rows without nonzeros are listed apart and zero-filled.
+//   scratch: partial rows of rows cut between work units, shared by the phases (they run
+//         in order on one stream).
 //
 // One step: the fetch streams (high priority) pull each peer's tiles — bulk tiles with one
 // copy-engine copy each (cudaMemcpyAsync over NVLink, as nvshmemx_getmem_on_stream in
 // src/comm_man.h:503), sparse tiles with one gather kernel per peer that moves the merged
 // needed rows with 128-bit loads from the peer's B (src/comm_man.h:72-101) — while the
-// compute stream runs segment 0, then waits for peer k's fetch event before segment k.
+// compute stream runs phase 0, then phase k as soon as the fetches of ring positions 1..k
+// have landed. The reference instead accumulates every tile into C (beta = 1,
+// src/dist_spmm_node.cu:371-383): one read-modify-write of C per tile, which phases avoid.
 #include <cuda_runtime.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include "device.cuh"
@@ -100,7 +104,13 @@ int launch_gather_rows(float *dst, const float *src, const int32_t *rows, int64_
   if (n <= 0) return DSP_OK;
   const bool v4 = dims % 4 == 0 && ((uintptr_t)dst & 15) == 0 && ((uintptr_t)src & 15) == 0;
   const int64_t warps_needed = (n + 3) / 4;
-  const int64_t blocks = std::min<int64_t>((warps_needed + 7) / 8, 148 * 8);
+  // the gather shares the SMs with the SpMM segments: cap its grid (NVLink, not the SMs,
+  // bounds it once a few hundred rows are in flight)
+  static const int64_t cap = [] {
+    const char *e = getenv("DSP_FETCH_BLOCKS");
+    return e ? std::max<int64_t>(1, atoll(e)) : (int64_t)148 * 8;
+  }();
+  const int64_t blocks = std::min<int64_t>((warps_needed + 7) / 8, cap);
   if (v4)
     gather_rows_v4_kernel<4><<<(unsigned)blocks, 256, 0, s>>>(dst, src, rows, n, dims, dims / 4);
   else
@@ -122,10 +132,12 @@ struct dsp_rank {
   int64_t scratch_floats = 0;
 
   struct Segment {
-    int owner = 0;
-    DevOperand op;
+    int owner = 0;  // (me + k) % P
+    DevOperand op;  // the rows of phase k
   };
-  std::vector<Segment> segs;  // segs[k].owner == (me + k) % P
+  std::vector<Segment> segs;  // one per phase / ring position k
+  int32_t *d_empty = nullptr;  // local rows without nonzeros (zero-filled each step)
+  int64_t n_empty = 0;
 
   struct Fetch {
     std::vector<std::pair<int64_t, int64_t>> bulk;  // (first row, rows)
@@ -142,52 +154,62 @@ struct dsp_rank {
   cudaStream_t compute = nullptr;
   std::vector<cudaStream_t> fstreams;
   cudaEvent_t ev_start = nullptr, ev_c0 = nullptr, ev_c1 = nullptr;
-  std::vector<cudaEvent_t> ev_fetch;
+  std::vector<cudaEvent_t> ev_fetch, ev_fetch_begin, ev_seg_begin, ev_seg_end;  // per peer / segment
+  std::vector<bool> fetch_ran, seg_ran;                                         // last step
   dsp_rank_stats stats{};
 };
 
 namespace {
 
-int build_segments(dsp_rank *r, const dsp_csr *a) {
+// Phase of every local row: the latest ring position (owner - me mod P) among its
+// columns' tiles; -1 for rows without nonzeros. Phase k holds whole rows, so each row is
+// computed once, with all its nonzeros, after the fetches of ring positions 1..k.
+int build_phases(dsp_rank *r, const dsp_csr *a) {
   const int P = r->P, me = r->me;
   const int64_t m = a->num_rows, cpt = r->cpt;
-  auto seg_of = [&](int64_t c) { return (r->remap[(size_t)(c / cpt)] - me + P) % P; };
+  std::vector<int32_t> phase((size_t)std::max<int64_t>(m, 1), -1);
+  parallel_for(m, [&](int64_t b, int64_t e) {
+    for (int64_t i = b; i < e; ++i) {
+      int32_t ph = -1;
+      for (int64_t j = a->indptr[i]; j < a->indptr[i + 1]; ++j)
+        ph = std::max<int32_t>(ph, (r->remap[(size_t)(a->indices[j] / cpt)] - me + P) % P);
+      phase[(size_t)i] = ph;
+    }
+  }, 1024);
+  std::vector<int32_t> empty;
+  for (int64_t i = 0; i < m; ++i)
+    if (phase[(size_t)i] < 0) empty.push_back((int32_t)i);
+  r->n_empty = (int64_t)empty.size();
+  if (r->n_empty) {
+    int rc = dev_upload(&r->d_empty, empty.data(), sizeof(int32_t) * empty.size());
+    if (rc) return rc;
+  }
   r->segs.resize((size_t)P);
   for (int k = 0; k < P; ++k) {
     auto &S = r->segs[(size_t)k];
     S.owner = (me + k) % P;
-    std::vector<int64_t> cnt((size_t)m + 1, 0);
-    parallel_for(m, [&](int64_t b, int64_t e) {
-      for (int64_t i = b; i < e; ++i) {
-        int64_t n = 0;
-        for (int64_t j = a->indptr[i]; j < a->indptr[i + 1]; ++j) n += seg_of(a->indices[j]) == k;
-        cnt[(size_t)i] = n;
-      }
-    }, 1024);
     std::vector<int32_t> rows;
+    std::vector<int64_t> src;  // first nonzero of each listed row in the local CSR
     std::vector<int64_t> ptr(1, 0);
     for (int64_t i = 0; i < m; ++i) {
-      if (k > 0 && cnt[(size_t)i] == 0) continue;
+      if (phase[(size_t)i] != k) continue;
       rows.push_back((int32_t)i);
-      ptr.push_back(ptr.back() + cnt[(size_t)i]);
+      src.push_back(a->indptr[i]);
+      ptr.push_back(ptr.back() + (a->indptr[i + 1] - a->indptr[i]));
     }
     const int64_t nr = (int64_t)rows.size(), nz = ptr.back();
     std::vector<int64_t> idx((size_t)std::max<int64_t>(nz, 1));
     std::vector<float> val((size_t)std::max<int64_t>(nz, 1));
     parallel_for(nr, [&](int64_t b, int64_t e) {
       for (int64_t q = b; q < e; ++q) {
-        const int64_t i = rows[(size_t)q];
-        int64_t p = ptr[(size_t)q];
-        for (int64_t j = a->indptr[i]; j < a->indptr[i + 1]; ++j)
-          if (seg_of(a->indices[j]) == k) {
-            idx[(size_t)p] = a->indices[j];
-            val[(size_t)p] = a->values[j];
-            ++p;
-          }
+        const int64_t n = ptr[(size_t)q + 1] - ptr[(size_t)q];
+        memcpy(&idx[(size_t)ptr[(size_t)q]], a->indices + src[(size_t)q], sizeof(int64_t) * (size_t)n);
+        memcpy(&val[(size_t)ptr[(size_t)q]], a->values + src[(size_t)q], sizeof(float) * (size_t)n);
       }
     }, 1024);
-    int rc = S.op.upload(r->device, m, r->M, ptr.data(), k == 0 ? nullptr : rows.data(), nr, idx.data(),
-                         val.data(), 0, nz, r->dims, k == 0);
+    // non-accumulating, but only the listed rows: no zero fill of the rows in between
+    int rc = S.op.upload(r->device, m, r->M, ptr.data(), rows.data(), nr, idx.data(), val.data(), 0, nz, r->dims,
+                         false);
     if (rc) return rc;
     r->scratch_floats = std::max(r->scratch_floats, S.op.pieces * (int64_t)r->dims);
   }
@@ -279,7 +301,7 @@ extern "C" int dsp_rank_create(const dsp_rank_desc *d, dsp_rank **out) {
     return bail(fail(DSP_ERR_NOMEM, "B (%zu bytes): %s", bbytes, cudaGetErrorString(e)));
   if ((e = cudaMalloc(&r->C, cbytes)) != cudaSuccess)
     return bail(fail(DSP_ERR_NOMEM, "C (%zu bytes): %s", cbytes, cudaGetErrorString(e)));
-  if ((rc = build_segments(r, d->local))) return bail(rc);
+  if ((rc = build_phases(r, d->local))) return bail(rc);
   if (r->P > 1 && (rc = build_fetch(r, d))) return bail(rc);
   if (r->scratch_floats > 0 && (e = cudaMalloc(&r->scratch, sizeof(float) * (size_t)r->scratch_floats)) != cudaSuccess)
     return bail(fail(DSP_ERR_NOMEM, "scratch: %s", cudaGetErrorString(e)));
@@ -296,10 +318,11 @@ extern "C" int dsp_rank_create(const dsp_rank_desc *d, dsp_rank **out) {
   if (cudaEventCreate(&r->ev_start) != cudaSuccess || cudaEventCreate(&r->ev_c0) != cudaSuccess ||
       cudaEventCreate(&r->ev_c1) != cudaSuccess)
     return bail(fail(DSP_ERR_CUDA, "event create failed"));
-  r->ev_fetch.assign((size_t)r->P, nullptr);
-  for (int k = 1; k < r->P; ++k)
-    if (cudaEventCreateWithFlags(&r->ev_fetch[(size_t)k], cudaEventDisableTiming) != cudaSuccess)
-      return bail(fail(DSP_ERR_CUDA, "event create failed"));
+  for (auto *v : {&r->ev_fetch, &r->ev_fetch_begin, &r->ev_seg_begin, &r->ev_seg_end}) {
+    v->assign((size_t)r->P, nullptr);
+    for (int k = 0; k < r->P; ++k)
+      if (cudaEventCreate(&(*v)[(size_t)k]) != cudaSuccess) return bail(fail(DSP_ERR_CUDA, "event create failed"));
+  }
 
   // statistics
   auto &s = r->stats;
@@ -307,11 +330,12 @@ extern "C" int dsp_rank_create(const dsp_rank_desc *d, dsp_rank **out) {
   s.nnz_local = r->nnz_local;
   s.segments = 0;
   s.launches_per_step = 0;
+  s.kernels_per_step = r->n_empty > 0;
   for (int k = 0; k < r->P; ++k) {
     const auto &op = r->segs[(size_t)k].op;
-    if (k == 0 || op.units() > 0) {
+    if (op.units() > 0) {
       s.segments++;
-      s.kernels_per_step += (op.units() > 0) + (op.n_split > 0);
+      s.kernels_per_step += 1 + (op.n_split > 0);
     }
     if (k > 0) {
       s.kernels_per_step += r->fetch[(size_t)k].n_rows > 0;
@@ -345,12 +369,14 @@ extern "C" void dsp_rank_destroy(dsp_rank *r) {
   if (r->B) cudaFree(r->B);
   if (r->C) cudaFree(r->C);
   if (r->scratch) cudaFree(r->scratch);
+  if (r->d_empty) cudaFree(r->d_empty);
   for (auto s : r->fstreams) cudaStreamDestroy(s);
   if (r->compute) cudaStreamDestroy(r->compute);
   for (auto ev : {r->ev_start, r->ev_c0, r->ev_c1})
     if (ev) cudaEventDestroy(ev);
-  for (auto ev : r->ev_fetch)
-    if (ev) cudaEventDestroy(ev);
+  for (auto *v : {&r->ev_fetch, &r->ev_fetch_begin, &r->ev_seg_begin, &r->ev_seg_end})
+    for (auto ev : *v)
+      if (ev) cudaEventDestroy(ev);
   cudaGetLastError();
   delete r;
 }
@@ -479,6 +505,7 @@ extern "C" int dsp_rank_step(dsp_rank *r, void *stream_v) {
     if (!F.n_rows && F.bulk.empty()) continue;
     cudaStream_t fs = r->fstreams[(size_t)((k - 1) % r->n_streams)];
     const float *src = r->peer_B[(size_t)r->segs[(size_t)k].owner];
+    DSP_CUDA(cudaEventRecord(r->ev_fetch_begin[(size_t)k], fs));
     for (const auto &b : F.bulk) {
       const size_t off = (size_t)b.first * r->dims;
       DSP_CUDA(cudaMemcpyAsync(r->B + off, src + off, sizeof(float) * (size_t)b.second * r->dims, cudaMemcpyDefault,
@@ -489,15 +516,24 @@ extern "C" int dsp_rank_step(dsp_rank *r, void *stream_v) {
     DSP_CUDA(cudaEventRecord(r->ev_fetch[(size_t)k], fs));
     has_fetch[(size_t)k] = true;
   }
-  // compute: own segment writes C, every later segment accumulates after its fetch
+  // compute: empty rows, then phase k once the fetches of ring positions 1..k landed; every
+  // row of C is written once (no accumulation)
   DSP_CUDA(cudaEventRecord(r->ev_c0, r->compute));
+  int rc = launch_zero_rows(r->C, r->dims, r->d_empty, r->n_empty, r->dims, r->compute);
+  if (rc) return rc;
+  r->seg_ran.assign((size_t)r->P, false);
+  int waited = 0;
   for (int k = 0; k < r->P; ++k) {
     const auto &op = r->segs[(size_t)k].op;
-    if (k > 0 && op.units() == 0) continue;
-    if (has_fetch[(size_t)k]) DSP_CUDA(cudaStreamWaitEvent(r->compute, r->ev_fetch[(size_t)k], 0));
-    int rc = launch_spmm(op.args(r->B, r->dims, r->C, r->dims, r->dims, r->scratch), k > 0, r->compute);
-    if (rc) return rc;
+    if (op.units() == 0) continue;
+    for (; waited < k; ++waited)
+      if (has_fetch[(size_t)waited + 1]) DSP_CUDA(cudaStreamWaitEvent(r->compute, r->ev_fetch[(size_t)waited + 1], 0));
+    DSP_CUDA(cudaEventRecord(r->ev_seg_begin[(size_t)k], r->compute));
+    if ((rc = launch_spmm(op.args(r->B, r->dims, r->C, r->dims, r->dims, r->scratch), false, r->compute))) return rc;
+    DSP_CUDA(cudaEventRecord(r->ev_seg_end[(size_t)k], r->compute));
+    r->seg_ran[(size_t)k] = true;
   }
+  r->fetch_ran = has_fetch;
   DSP_CUDA(cudaEventRecord(r->ev_c1, r->compute));
   for (int k = 1; k < r->P; ++k)
     if (has_fetch[(size_t)k]) DSP_CUDA(cudaStreamWaitEvent(stream, r->ev_fetch[(size_t)k], 0));
@@ -509,5 +545,23 @@ extern "C" int dsp_rank_last_compute_ms(dsp_rank *r, float *ms) {
   DSP_TRY_ARG(r && ms, "dsp_rank_last_compute_ms: null argument");
   DeviceGuard g(r->device);
   DSP_CUDA(cudaEventElapsedTime(ms, r->ev_c0, r->ev_c1));
+  return DSP_OK;
+}
+
+extern "C" int dsp_rank_last_timeline(dsp_rank *r, float *ms, int cap) {
+  DSP_TRY_ARG(r && ms && cap >= 4 * r->P, "dsp_rank_last_timeline: need %d floats", r ? 4 * r->P : 0);
+  DeviceGuard g(r->device);
+  for (int k = 0; k < r->P; ++k) {
+    float *o = ms + 4 * k;
+    o[0] = o[1] = o[2] = o[3] = -1.f;
+    if (k < (int)r->fetch_ran.size() && r->fetch_ran[(size_t)k]) {
+      DSP_CUDA(cudaEventElapsedTime(&o[0], r->ev_start, r->ev_fetch_begin[(size_t)k]));
+      DSP_CUDA(cudaEventElapsedTime(&o[1], r->ev_start, r->ev_fetch[(size_t)k]));
+    }
+    if (k < (int)r->seg_ran.size() && r->seg_ran[(size_t)k]) {
+      DSP_CUDA(cudaEventElapsedTime(&o[2], r->ev_start, r->ev_seg_begin[(size_t)k]));
+      DSP_CUDA(cudaEventElapsedTime(&o[3], r->ev_start, r->ev_seg_end[(size_t)k]));
+    }
+  }
   return DSP_OK;
 }

@@ -225,7 +225,8 @@ __global__ void __launch_bounds__(kSpmmThreads) spmm_nnz_kernel(const SpmmArgs a
   int32_t row = a.coo_row[s];
   const int32_t head_row = row;
   // empty rows between the previous chunk's last row and this chunk's first row
-  if (!kAccum) zero_rows<LPR, VPL, W>(a, s > 0 ? (int64_t)a.coo_row[s - 1] + 1 : 0, row, col0);
+  // (only operands that list every output row, zero_rows > 0, own the rows in between)
+  if (!kAccum && a.zero_rows > 0) zero_rows<LPR, VPL, W>(a, s > 0 ? (int64_t)a.coo_row[s - 1] + 1 : 0, row, col0);
 
   constexpr int K = entries_per_lane<LPR>();
   T acc[VPL];
@@ -268,7 +269,7 @@ __global__ void __launch_bounds__(kSpmmThreads) spmm_nnz_kernel(const SpmmArgs a
           if (j + u < n) {
             if (ru[u] != row) {  // group-uniform: the chunk crosses into the next row
               flush_row<LPR, VPL, W, kAccum>(a, row, row == head_row ? head_slot : -1, col0, acc);
-              if (!kAccum) zero_rows<LPR, VPL, W>(a, (int64_t)row + 1, ru[u], col0);
+              if (!kAccum && a.zero_rows > 0) zero_rows<LPR, VPL, W>(a, (int64_t)row + 1, ru[u], col0);
               row = ru[u];
 #pragma unroll
               for (int w = 0; w < VPL; ++w) acc[w] = V::zero();
@@ -312,6 +313,15 @@ __global__ void fill_dense_kernel(float *B, int64_t row0, int64_t rows, int64_t 
        i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t r = i / ncols, c = i - r * ncols;
     B[r * ld + c] = dense_value(seed, row0 + r, c);
+  }
+}
+
+__global__ void zero_rows_kernel(float *C, int64_t ldc, const int32_t *rows, int64_t n, int N) {
+  const int lane = threadIdx.x & 31;
+  for (int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; i < n;
+       i += ((int64_t)gridDim.x * blockDim.x) >> 5) {
+    float *dst = C + (int64_t)__ldg(rows + i) * ldc;
+    for (int c = lane; c < N; c += 32) __stcs(dst + c, 0.f);
   }
 }
 
@@ -445,6 +455,14 @@ int launch_fill_dense(float *B, int64_t row0, int64_t rows, int64_t ld, int64_t 
   fill_dense_kernel<<<148 * 8, 256, 0, stream>>>(B, row0, rows, ld, ncols, seed);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? DSP_OK : fail(DSP_ERR_CUDA, "fill: %s", cudaGetErrorString(e));
+}
+
+int launch_zero_rows(float *C, int64_t ldc, const int32_t *rows, int64_t n, int N, cudaStream_t stream) {
+  if (n <= 0 || N <= 0) return DSP_OK;
+  const int64_t blocks = std::min<int64_t>((n + 7) / 8, 148 * 8);
+  zero_rows_kernel<<<(unsigned)blocks, 256, 0, stream>>>(C, ldc, rows, n, N);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? DSP_OK : fail(DSP_ERR_CUDA, "zero rows: %s", cudaGetErrorString(e));
 }
 
 int launch_fill_const(float *B, int64_t n, float v, cudaStream_t stream) {

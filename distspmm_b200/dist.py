@@ -130,6 +130,16 @@ class Rank:
         call("dsp_rank_last_compute_ms", self._h, ctypes.byref(ms))
         return float(ms.value)
 
+    def timeline(self) -> list:
+        """Last step: per ring position k, (fetch_begin, fetch_end, seg_begin, seg_end) in ms
+        from the step start (None where nothing ran)."""
+        buf = (c_f32 * (4 * self.world))()
+        call("dsp_rank_last_timeline", self._h, buf, 4 * self.world)
+        out = []
+        for k in range(self.world):
+            out.append(tuple(None if buf[4 * k + i] < 0 else round(float(buf[4 * k + i]), 4) for i in range(4)))
+        return out
+
     def stats(self) -> dict:
         s = dsp_rank_stats()
         call("dsp_rank_stats_get", self._h, ctypes.byref(s))

@@ -316,6 +316,11 @@ int dsp_rank_download_c(dsp_rank *r, float *C_host, void *stream);
 /* Device time (ms) of the SpMM kernels of the last step, from CUDA events on the compute
  * stream (valid after the step completed). */
 int dsp_rank_last_compute_ms(dsp_rank *r, float *ms);
+/* Timeline of the last step (valid after it completed), ms from the step's start, 4 floats
+ * per ring position k = 0..P-1: fetch begin, fetch end (peer (me+k)%P), segment begin,
+ * segment end; -1 where nothing ran. cap >= 4*P. Shows how much of the fetch the SpMM
+ * segments hid (the reference measures only whole reps, src/dist_spmm_node.cu:329-394). */
+int dsp_rank_last_timeline(dsp_rank *r, float *ms, int cap);
 
 /* ---------------------------------------------------------------- whole pipeline */
 /* The dist_spmm_node program (src/dist_spmm_node.cu:20-444) run in one process that
