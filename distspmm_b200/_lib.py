@@ -54,7 +54,8 @@ class dsp_rank_desc(ctypes.Structure):
     _fields_ = [("rank", c_int), ("world", c_int), ("device", c_int), ("dims", c_int), ("T", c_int),
                 ("n_streams", c_int), ("cpt", c_i64), ("M", c_i64), ("m_lb", c_i64),
                 ("local", P(dsp_csr)), ("remap", P(c_i32)), ("sparse", P(ctypes.c_uint8)),
-                ("needed_offsets", P(c_i64)), ("needed_cols", P(c_i32)), ("n_slice", P(c_i32))]
+                ("needed_offsets", P(c_i64)), ("needed_cols", P(c_i32)), ("n_slice", P(c_i32)),
+                ("fetch_engine", c_int)]
 
 
 class dsp_rank_stats(ctypes.Structure):
@@ -127,6 +128,8 @@ PROTOTYPES = {
     "dsp_rank_upload_b": (c_int, [c_vp, c_vp, c_vp]),
     "dsp_rank_poison_remote": (c_int, [c_vp, c_vp]),
     "dsp_rank_step": (c_int, [c_vp, c_vp]),
+    "dsp_rank_check_error": (c_int, [c_vp]),
+    "dsp_selftest_bounded_wait": (c_int, [ctypes.c_longlong, P(c_int)]),
     "dsp_rank_download_c": (c_int, [c_vp, c_vp, c_vp]),
     "dsp_rank_last_compute_ms": (c_int, [c_vp, P(c_f32)]),
     "dsp_rank_last_timeline": (c_int, [c_vp, P(c_f32), c_int]),

@@ -56,6 +56,10 @@ int launch_spmm(const SpmmArgs &a, bool accumulate, cudaStream_t stream);
 int launch_fill_dense(float *B, int64_t row0, int64_t rows, int64_t ld, int64_t ncols, uint64_t seed,
                       cudaStream_t stream);
 int launch_fill_const(float *B, int64_t n, float v, cudaStream_t stream);
+// dst[r, :] = src[r, :] for the global rows r = rows[0..n) (src: a peer's B). A wait that
+// gives up sets *err (non-zero) instead of hanging.
+int launch_gather_rows(float *dst, const float *src, const int32_t *rows, int64_t n, int dims, int engine, int *err,
+                       cudaStream_t s);
 // C[rows[i], 0:N] = 0 for i < n.
 int launch_zero_rows(float *C, int64_t ldc, const int32_t *rows, int64_t n, int N, cudaStream_t stream);
 void prefer_l1_carveout();

@@ -53,78 +53,14 @@ struct DeviceGuard {
     if (e_ != cudaSuccess) return fail(DSP_ERR_CUDA, "%s: %s", #call, cudaGetErrorString(e_)); \
   } while (0)
 
-__device__ __forceinline__ float4 ld_peer_v4(const float *p) {
-  float4 v;
-  asm volatile("ld.global.L1::no_allocate.v4.f32 {%0,%1,%2,%3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "l"(p));
-  return v;
-}
-
-// Sparsity-aware fetch: dst[r, :] = src[r, :] for every global row r in rows[0..n).
-// One warp per group of kRows rows; all loads of the group are issued before the stores.
-template <int kRows>
-__global__ void __launch_bounds__(256) gather_rows_v4_kernel(float *__restrict__ dst, const float *__restrict__ src,
-                                                             const int32_t *__restrict__ rows, int64_t n,
-                                                             int64_t ld, int nvec) {
-  const int lane = threadIdx.x & 31;
-  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-  for (int64_t g = warp * kRows; g < n; g += nwarps * kRows) {
-    int32_t r[kRows];
-#pragma unroll
-    for (int k = 0; k < kRows; ++k) r[k] = g + k < n ? __ldg(rows + g + k) : -1;
-    for (int v = lane; v < nvec; v += 32) {
-      float4 x[kRows];
-#pragma unroll
-      for (int k = 0; k < kRows; ++k)
-        if (r[k] >= 0) x[k] = ld_peer_v4(src + (int64_t)r[k] * ld + 4 * v);
-#pragma unroll
-      for (int k = 0; k < kRows; ++k)
-        if (r[k] >= 0) *reinterpret_cast<float4 *>(dst + (int64_t)r[k] * ld + 4 * v) = x[k];
-    }
-  }
-}
-
-__global__ void __launch_bounds__(256) gather_rows_f1_kernel(float *__restrict__ dst, const float *__restrict__ src,
-                                                             const int32_t *__restrict__ rows, int64_t n,
-                                                             int64_t ld, int dims) {
-  const int lane = threadIdx.x & 31;
-  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-  for (int64_t g = warp; g < n; g += nwarps) {
-    const int64_t r = __ldg(rows + g);
-    for (int c = lane; c < dims; c += 32) dst[r * ld + c] = src[r * ld + c];
-  }
-}
-
 }  // namespace
-
-int launch_gather_rows(float *dst, const float *src, const int32_t *rows, int64_t n, int dims, cudaStream_t s) {
-  if (n <= 0) return DSP_OK;
-  const bool v4 = dims % 4 == 0 && ((uintptr_t)dst & 15) == 0 && ((uintptr_t)src & 15) == 0;
-  const int64_t warps_needed = (n + 3) / 4;
-  // the gather shares the SMs with the SpMM segments: cap its grid (NVLink, not the SMs,
-  // bounds it once a few hundred rows are in flight)
-  static const int64_t cap = [] {
-    const char *e = getenv("DSP_FETCH_BLOCKS");
-    return e ? std::max<int64_t>(1, atoll(e)) : (int64_t)148 * 8;
-  }();
-  const int64_t blocks = std::min<int64_t>((warps_needed + 7) / 8, cap);
-  if (v4)
-    gather_rows_v4_kernel<4><<<(unsigned)blocks, 256, 0, s>>>(dst, src, rows, n, dims, dims / 4);
-  else
-    gather_rows_f1_kernel<<<(unsigned)blocks, 256, 0, s>>>(dst, src, rows, n, dims, dims);
-  cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? DSP_OK : fail(DSP_ERR_CUDA, "gather launch: %s", cudaGetErrorString(e));
-}
-
 }  // namespace dsp
 
 using namespace dsp;
 
 struct dsp_rank {
-  int me = 0, P = 1, device = 0, dims = 0, T = 0, n_streams = 1;
+  int me = 0, P = 1, device = 0, dims = 0, T = 0, n_streams = 1, fetch_engine = DSP_FETCH_LSU;
+  int *d_err = nullptr;  // set by a fetch kernel whose bounded wait gave up
   int64_t cpt = 0, M = 0, m_lb = 0, m_local = 0, nnz_local = 0;
   std::vector<int32_t> remap;
   std::vector<uint8_t> sparse;
@@ -275,6 +211,7 @@ extern "C" int dsp_rank_create(const dsp_rank_desc *d, dsp_rank **out) {
   r->dims = d->dims;
   r->T = d->T;
   r->n_streams = std::max(1, d->n_streams);
+  r->fetch_engine = d->fetch_engine == DSP_FETCH_TMA ? DSP_FETCH_TMA : DSP_FETCH_LSU;
   r->cpt = d->cpt;
   r->M = d->M;
   r->m_lb = d->m_lb;
@@ -301,6 +238,8 @@ extern "C" int dsp_rank_create(const dsp_rank_desc *d, dsp_rank **out) {
     return bail(fail(DSP_ERR_NOMEM, "B (%zu bytes): %s", bbytes, cudaGetErrorString(e)));
   if ((e = cudaMalloc(&r->C, cbytes)) != cudaSuccess)
     return bail(fail(DSP_ERR_NOMEM, "C (%zu bytes): %s", cbytes, cudaGetErrorString(e)));
+  if ((e = cudaMalloc(&r->d_err, sizeof(int))) != cudaSuccess || (e = cudaMemset(r->d_err, 0, sizeof(int))) != cudaSuccess)
+    return bail(fail(DSP_ERR_NOMEM, "error flag: %s", cudaGetErrorString(e)));
   if ((rc = build_phases(r, d->local))) return bail(rc);
   if (r->P > 1 && (rc = build_fetch(r, d))) return bail(rc);
   if (r->scratch_floats > 0 && (e = cudaMalloc(&r->scratch, sizeof(float) * (size_t)r->scratch_floats)) != cudaSuccess)
@@ -370,6 +309,7 @@ extern "C" void dsp_rank_destroy(dsp_rank *r) {
   if (r->C) cudaFree(r->C);
   if (r->scratch) cudaFree(r->scratch);
   if (r->d_empty) cudaFree(r->d_empty);
+  if (r->d_err) cudaFree(r->d_err);
   for (auto s : r->fstreams) cudaStreamDestroy(s);
   if (r->compute) cudaStreamDestroy(r->compute);
   for (auto ev : {r->ev_start, r->ev_c0, r->ev_c1})
@@ -511,7 +451,7 @@ extern "C" int dsp_rank_step(dsp_rank *r, void *stream_v) {
       DSP_CUDA(cudaMemcpyAsync(r->B + off, src + off, sizeof(float) * (size_t)b.second * r->dims, cudaMemcpyDefault,
                                fs));
     }
-    int rc = launch_gather_rows(r->B, src, F.d_rows, F.n_rows, r->dims, fs);
+    int rc = launch_gather_rows(r->B, src, F.d_rows, F.n_rows, r->dims, r->fetch_engine, r->d_err, fs);
     if (rc) return rc;
     DSP_CUDA(cudaEventRecord(r->ev_fetch[(size_t)k], fs));
     has_fetch[(size_t)k] = true;
@@ -539,6 +479,16 @@ extern "C" int dsp_rank_step(dsp_rank *r, void *stream_v) {
     if (has_fetch[(size_t)k]) DSP_CUDA(cudaStreamWaitEvent(stream, r->ev_fetch[(size_t)k], 0));
   DSP_CUDA(cudaStreamWaitEvent(stream, r->ev_c1, 0));
   return DSP_OK;
+}
+
+extern "C" int dsp_rank_check_error(dsp_rank *r) {
+  DSP_TRY_ARG(r, "dsp_rank_check_error: null rank");
+  DeviceGuard g(r->device);
+  int flag = 0;
+  DSP_CUDA(cudaMemcpy(&flag, r->d_err, sizeof flag, cudaMemcpyDeviceToHost));
+  if (flag == 0) return DSP_OK;
+  DSP_CUDA(cudaMemset(r->d_err, 0, sizeof(int)));
+  return fail(DSP_ERR_TIMEOUT, "rank %d: a fetch wait gave up (code %d); the step's C is incomplete", r->me, flag);
 }
 
 extern "C" int dsp_rank_last_compute_ms(dsp_rank *r, float *ms) {

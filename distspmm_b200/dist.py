@@ -51,11 +51,15 @@ def global_plan(tilings: list, task_dist: int, n_rolls: int) -> GlobalPlan:
 
 # ---------------------------------------------------------------------------- rank
 
+FETCH_ENGINES = {"lsu": 0, "tma": 1}  # DSP_FETCH_LSU / DSP_FETCH_TMA
+
+
 class Rank:
     """A dsp_rank: one GPU's segments, B / C buffers, fetch plan and streams."""
 
     def __init__(self, local: Csr, rank: int, world: int, device: int, dims: int, M: int, m_lb: int,
-                 plan: GlobalPlan, n_slice: np.ndarray, sparse: np.ndarray, n_streams: int = 4):
+                 plan: GlobalPlan, n_slice: np.ndarray, sparse: np.ndarray, n_streams: int = 4,
+                 fetch_engine: str = "lsu"):
         self.rank, self.world, self.device, self.dims, self.M = rank, world, device, dims, M
         self.m_local = local.num_rows
         self.m_lb = m_lb
@@ -73,6 +77,7 @@ class Rank:
         d.needed_offsets = plan.offsets.ctypes.data_as(P(c_i64))
         d.needed_cols = merged.ctypes.data_as(P(c_i32))
         d.n_slice = self._keep[2].ctypes.data_as(P(c_i32))
+        d.fetch_engine = FETCH_ENGINES[fetch_engine]
         h = c_vp()
         call("dsp_rank_create", ctypes.byref(d), ctypes.byref(h))
         self._h = h
@@ -118,6 +123,10 @@ class Rank:
     def step(self, stream: int = 0) -> None:
         call("dsp_rank_step", self._h, stream)
 
+    def check_error(self) -> None:
+        """Raise DspError(DSP_ERR_TIMEOUT) if a fetch wait of an earlier step gave up."""
+        call("dsp_rank_check_error", self._h)
+
     def download_c(self, C_host: np.ndarray, stream: int = 0) -> None:
         assert C_host.dtype == np.float32 and C_host.flags.c_contiguous and C_host.shape == (self.m_local, self.dims)
         call("dsp_rank_download_c", self._h, C_host.ctypes.data, stream)
@@ -158,10 +167,11 @@ class Rank:
 
 
 def make_rank(local: Csr, rank: int, world: int, device: int, dims: int, M: int, m_lb: int, tiling,
-              plan: GlobalPlan, comm_type: int, platform: str = "h100", n_streams: int = 4) -> Rank:
+              plan: GlobalPlan, comm_type: int, platform: str = "h100", n_streams: int = 4,
+              fetch_engine: str = "lsu") -> Rank:
     """Selector (CommMan_hp ctor, src/comm_man.h:341-410) + rank construction."""
     sparse = planner.comm_select(comm_type, dims, plan.n_col, tiling.n_slice, platform)
-    r = Rank(local, rank, world, device, dims, M, m_lb, plan, tiling.n_slice, sparse, n_streams)
+    r = Rank(local, rank, world, device, dims, M, m_lb, plan, tiling.n_slice, sparse, n_streams, fetch_engine)
     r.sparse = sparse
     r.n_slice = tiling.n_slice
     return r
@@ -191,7 +201,8 @@ class LocalGroup:
 
 
 def build_local_group(g: Csr, world: int, devices, dims: int, n_rolls: int = 4, task_dist: int = 2,
-                      comm_type: int = 2, platform: str = "h100", n_streams: int = 4) -> LocalGroup:
+                      comm_type: int = 2, platform: str = "h100", n_streams: int = 4,
+                      fetch_engine: str = "lsu") -> LocalGroup:
     """All `world` ranks of the pipeline in this process; devices[p] is rank p's GPU
     (ranks may share one). Peers read each other's B directly (same device, or peer
     access between devices)."""
@@ -202,7 +213,7 @@ def build_local_group(g: Csr, world: int, devices, dims: int, n_rolls: int = 4, 
     tilings = [planner.tile(loc, T) for loc in locals_]
     plan = global_plan(tilings, task_dist, n_rolls)
     ranks = [make_rank(locals_[p], p, world, devices[p], dims, M, bounds[p][0], tilings[p], plan, comm_type,
-                       platform, n_streams) for p in range(world)]
+                       platform, n_streams, fetch_engine) for p in range(world)]
     for p in range(world):
         for q in range(world):
             if p != q:

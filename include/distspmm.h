@@ -271,7 +271,13 @@ typedef struct dsp_rank_desc {
   const int64_t *needed_offsets; /* [T+1] merged needed lists                   */
   const int32_t *needed_cols;    /* tile-local ids, ascending per tile          */
   const int32_t *n_slice;        /* [T] n_slice_list of this rank               */
+  int fetch_engine;              /* DSP_FETCH_LSU (default) or DSP_FETCH_TMA     */
 } dsp_rank_desc;
+
+/* Sparse-fetch engines: LSU = warps with 128-bit peer loads, one block per SM next to the
+ * SpMM; TMA = per-row cp.async.bulk copies through a shared-memory ring (no multicast). */
+#define DSP_FETCH_LSU 0
+#define DSP_FETCH_TMA 1
 
 typedef struct dsp_rank_stats {
   int64_t m_local, nnz_local;
@@ -311,6 +317,15 @@ int dsp_rank_upload_b(dsp_rank *r, const float *B_host, void *stream);
  * `stream`; later work on `stream` is ordered after it. Peers' owned tiles must hold the
  * step's B before the call (the caller's barrier). */
 int dsp_rank_step(dsp_rank *r, void *stream);
+/* After the step's stream was synchronised: DSP_OK, or DSP_ERR_TIMEOUT if a fetch kernel's
+ * bounded wait on its bulk copies gave up during an earlier step (the flag is cleared).
+ * The reference has no failure detection (src/utils.h:26-84 exit() on any error). */
+int dsp_rank_check_error(dsp_rank *r);
+/* Test of the fetch kernels' bounded wait on the current device: one CTA waits on an
+ * mbarrier that nothing arrives at, for budget_cycles clock64 cycles (<= ~2 s), then
+ * records code 3 and returns. Returns DSP_ERR_TIMEOUT with *code_out = 3 when the wait gave
+ * up as designed, DSP_OK if it (impossibly) completed. No fault, no hang. */
+int dsp_selftest_bounded_wait(long long budget_cycles, int *code_out);
 /* Copy C (m_local x dims) to host. */
 int dsp_rank_download_c(dsp_rank *r, float *C_host, void *stream);
 /* Device time (ms) of the SpMM kernels of the last step, from CUDA events on the compute

@@ -23,10 +23,10 @@ def _devices(world):
     return [p % n for p in range(world)]
 
 
-def _run_group(A, world, dims, rolls, task_dist, comm_type, seed=21, poison=True):
+def _run_group(A, world, dims, rolls, task_dist, comm_type, seed=21, poison=True, fetch_engine="lsu"):
     import torch
     from distspmm_b200.dist import build_local_group
-    g = build_local_group(A, world, _devices(world), dims, rolls, task_dist, comm_type)
+    g = build_local_group(A, world, _devices(world), dims, rolls, task_dist, comm_type, fetch_engine=fetch_engine)
     for r in g.ranks:
         if poison:
             r.poison_remote()
@@ -36,6 +36,8 @@ def _run_group(A, world, dims, rolls, task_dist, comm_type, seed=21, poison=True
     g.step()
     for dev in set(_devices(world)):
         torch.cuda.synchronize(dev)
+    for r in g.ranks:
+        r.check_error()  # no fetch wait gave up
     C = np.zeros((A.num_rows, dims), np.float32)
     for r, (lb, ub) in zip(g.ranks, g.bounds):
         if ub > lb:
@@ -79,6 +81,17 @@ def test_group_parity_rmat(gpu, rmat12, world, rolls, task_dist, comm_type):
                 continue
             exp += g.plan.n_col[t] if r.sparse[t] else g.tilings[p].n_slice[t]
         assert s["fetch_rows"] == exp
+    g.close()
+
+
+@pytest.mark.parametrize("engine", ["lsu", "tma"])
+@pytest.mark.parametrize("dims", [4, 128, 100, 1024])
+def test_group_parity_fetch_engines(gpu, rmat12, engine, dims):
+    """Both sparse-fetch engines (TMA needs 16-byte rows; dims = 100 and other odd widths use
+    the vector or scalar gather instead)."""
+    g, C = _run_group(rmat12, 4, dims, 2, 2, 1, fetch_engine=engine)
+    _check(rmat12, C, dims)
+    assert all(r.stats()["fetch_sparse_tiles"] > 0 for r in g.ranks)
     g.close()
 
 
@@ -165,3 +178,18 @@ def test_cli_report_format(gpu, tmp_path):
     # usage error and .mtx refusal as in the reference
     assert subprocess.run([exe, prefix], capture_output=True).returncode != 0
     assert subprocess.run([exe, "x.mtx", "64", "2", "2", "2", "7"], capture_output=True).returncode != 0
+
+
+def test_bounded_wait_gives_up_with_a_status(gpu):
+    """Failure detection without a fault: a fetch-style wait on an mbarrier that nothing
+    completes gives up after its budget, records an error code the host reads, and leaves
+    the context usable."""
+    import ctypes
+
+    import torch
+    from distspmm_b200 import _lib
+    code = ctypes.c_int(0)
+    rc = _lib.lib().dsp_selftest_bounded_wait(2_000_000, ctypes.byref(code))  # ~1 ms budget
+    assert rc == -7 and code.value == 3
+    assert b"gave up" in _lib.lib().dsp_last_error()
+    assert (torch.ones(4, device="cuda") * 2).sum().item() == 8
