@@ -46,7 +46,7 @@ UNIT = "GFLOPS"
 def parse_args(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--matrix", choices=["rmat", "stencil27", "uniform"], default="rmat",
@@ -126,7 +126,7 @@ def measured_peaks():
 
 def profile_traffic(workload):
     """DRAM bytes per launch of the SpMM kernel from the committed ncu summary, if any."""
-    path = os.path.join(ROOT, "profiles", f"spmm_items_{workload}.md")
+    path = os.path.join(ROOT, "profiles", f"spmm_{workload}.md")
     try:
         txt = open(path).read()
     except OSError:
@@ -136,8 +136,8 @@ def profile_traffic(workload):
 
 
 class Clocks:
-    """nvidia-smi sampling during the timed region."""
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    """nvidia-smi sampling (every 50 ms) kept to the samples taken inside the timed region."""
+    Q = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -145,14 +145,22 @@ class Clocks:
         self.index = index
         self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
         self.p = None
+        self.t0 = self.t1 = None
 
     def start(self):
         try:
             self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
-                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                       "--format=csv,noheader,nounits", "-lms", "50"],
                                       stdout=self.f, stderr=subprocess.DEVNULL)
+            time.sleep(0.5)  # let the sampler come up before the timed region opens
         except OSError:
             self.p = None
+
+    def mark(self, begin: bool):
+        if begin:
+            self.t0 = datetime.datetime.now()
+        else:
+            self.t1 = datetime.datetime.now()
 
     def stop(self):
         if self.p is None:
@@ -163,14 +171,23 @@ class Clocks:
         except subprocess.TimeoutExpired:
             self.p.kill()
         self.f.seek(0)
-        rows = [r for r in csv.reader(io.StringIO(self.f.read())) if len(r) >= 9]
+        rows = [r for r in csv.reader(io.StringIO(self.f.read())) if len(r) >= 10]
         os.unlink(self.f.name)
+
+        def inside(r):
+            try:
+                ts = datetime.datetime.strptime(r[0].strip(), "%Y/%m/%d %H:%M:%S.%f")
+            except ValueError:
+                return False
+            return self.t0 is not None and self.t0 <= ts <= self.t1
+
+        rows = [r for r in rows if inside(r)]
         if not rows:
-            return None
-        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        sm = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
+        mx = [float(r[3]) for r in rows if r[3].strip().replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if "Active" in v and "Not" not in v})
+        reasons = sorted({n for r in rows for n, v in zip(names, r[6:10]) if "Active" in v and "Not" not in v})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
                 "reasons": reasons, "samples": len(rows)}
 
@@ -314,6 +331,8 @@ def main(argv=None):
     if comm is not None:
         comm.barrier()
     t_wall = time.perf_counter()
+    if clocks:
+        clocks.mark(True)
     for _ in range(a.steps):
         flush_l2()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -328,6 +347,8 @@ def main(argv=None):
     if comm is not None:
         comm.barrier()
     wall = time.perf_counter() - t_wall
+    if clocks:
+        clocks.mark(False)
     clk = clocks.stop() if clocks else None
 
     # compute-stream time spent waiting for fetches in the last step (segments not back to back)
@@ -396,6 +417,23 @@ def main(argv=None):
     if rank == 0 and world == 1 and not a.no_cpu_baseline and not a.profile:
         cpu = cpu_spmm_baseline(A, d.dense_b(M, a.dims, a.seed + 1))
 
+    # Gather roofline: every nonzero reads one B row of dims floats. The ceiling is the
+    # random-row gather bandwidth of this GPU over a buffer as large as B, measured here
+    # (outside the timed region) by the library's probe.
+    gather = None
+    if world == 1 and not a.profile:
+        import ctypes
+
+        from distspmm_b200 import _lib
+        pms, pgbs = ctypes.c_float(), ctypes.c_double()
+        _lib.call("dsp_probe_gather", M, a.dims, min(nnz, 1 << 25), 3, ctypes.byref(pms), ctypes.byref(pgbs))
+        gathered = nnz * a.dims * 4
+        ach = gathered / (mean_compute * 1e-3) / 1e9
+        gather = {"gathered_bytes_per_launch": gathered, "achieved": round(ach, 1), "ceiling": round(pgbs.value, 1),
+                  "unit": "GB/s", "frac": round(ach / pgbs.value, 4),
+                  "ceiling_source": f"dsp_probe_gather: {min(nnz, 1 << 25)} random {a.dims * 4}-byte rows of a "
+                                    f"{M}-row buffer"}
+
     fetch_bytes = st["fetch_bytes"]
     if comm is not None:
         fetch_bytes = comm.allreduce_sum_i64(fetch_bytes)
@@ -405,7 +443,7 @@ def main(argv=None):
         "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config_of(a, world, nnz, M),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": profile_traffic(workload_name(a)),
-                     "kernel": "spmm_items_kernel (+fixup)", "rank": rank,
+                     "kernel": "spmm_nnz_kernel / spmm_rows_kernel (+fixup, zero rows)", "rank": rank,
                      "alg_bytes_per_launch": alg_bytes, "launch_ms": round(mean_compute, 4),
                      "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})"},
         "e2e": e2e, "cpu_baseline": cpu, "clocks": clk,
@@ -415,6 +453,7 @@ def main(argv=None):
                    "max_rank_compute_idle_ms": round(idle_max, 4),
                    "timeline_rank0": timeline if rank == 0 else None},
         "wall_s_timed_region": round(wall, 3),
+        "gather": gather,
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
