@@ -417,22 +417,11 @@ def main(argv=None):
     if rank == 0 and world == 1 and not a.no_cpu_baseline and not a.profile:
         cpu = cpu_spmm_baseline(A, d.dense_b(M, a.dims, a.seed + 1))
 
-    # Gather roofline: every nonzero reads one B row of dims floats. The ceiling is the
-    # random-row gather bandwidth of this GPU over a buffer as large as B, measured here
-    # (outside the timed region) by the library's probe.
-    gather = None
-    if world == 1 and not a.profile:
-        import ctypes
-
-        from distspmm_b200 import _lib
-        pms, pgbs = ctypes.c_float(), ctypes.c_double()
-        _lib.call("dsp_probe_gather", M, a.dims, min(nnz, 1 << 25), 3, ctypes.byref(pms), ctypes.byref(pgbs))
-        gathered = nnz * a.dims * 4
-        ach = gathered / (mean_compute * 1e-3) / 1e9
-        gather = {"gathered_bytes_per_launch": gathered, "achieved": round(ach, 1), "ceiling": round(pgbs.value, 1),
-                  "unit": "GB/s", "frac": round(ach / pgbs.value, 4),
-                  "ceiling_source": f"dsp_probe_gather: {min(nnz, 1 << 25)} random {a.dims * 4}-byte rows of a "
-                                    f"{M}-row buffer"}
+    # Gather stream: every nonzero reads one B row of dims floats through L2 -> L1 (what
+    # bounds a gather-per-nonzero kernel, next to the HBM roofline's algorithmic bytes).
+    gathered = st["nnz_local"] * a.dims * 4
+    gather = {"gathered_bytes_per_launch": gathered, "unit": "GB/s",
+              "achieved": round(gathered / (mean_compute * 1e-3) / 1e9, 1)}
 
     fetch_bytes = st["fetch_bytes"]
     if comm is not None:

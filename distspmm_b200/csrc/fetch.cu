@@ -266,81 +266,3 @@ extern "C" int dsp_selftest_bounded_wait(long long budget_cycles, int *code_out)
   *code_out = v;
   return v != 0 ? dsp::fail(DSP_ERR_TIMEOUT, "bounded wait gave up as designed (code %d)", v) : DSP_OK;
 }
-
-// ------------------------------------------------------------------ gather-bandwidth probe
-//
-// The ceiling that bounds a gather-per-nonzero SpMM: every nonzero reads one whole B row
-// (row_floats x 4 bytes) at a column index the matrix decides. This probe reads n random
-// rows of a rows x row_floats buffer (one warp per row, float4 per lane, 8 rows in flight
-// per warp) and reports the bandwidth of the gathered bytes, for a working set the caller
-// picks (e.g. the size of B). It allocates its own buffers.
-
-namespace dsp {
-namespace {
-
-__global__ void __launch_bounds__(256) probe_gather_kernel(const float4 *__restrict__ buf,
-                                                           const int32_t *__restrict__ idx, int64_t n,
-                                                           int vec_per_row, float *sink) {
-  const int lane = threadIdx.x & 31;
-  const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
-  float acc = 0.f;
-  for (int64_t i = w * 8; i < n; i += nw * 8) {
-    float4 v[8];
-#pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int64_t r = i + u < n ? __ldg(idx + i + u) : 0;
-      v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int c = lane; c < vec_per_row; c += 32)
-        if (i + u < n) v[u] = __ldg(buf + r * vec_per_row + c);
-    }
-#pragma unroll
-    for (int u = 0; u < 8; ++u) acc += v[u].x + v[u].y + v[u].z + v[u].w;
-  }
-  if (acc == 1.2345e-30f) *sink = acc;  // keeps the loads alive
-}
-
-__global__ void probe_fill_kernel(int32_t *idx, int64_t n, int64_t rows, uint64_t seed) {
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
-    idx[i] = (int32_t)(mix64(seed ^ (uint64_t)i) % (uint64_t)rows);
-}
-
-}  // namespace
-}  // namespace dsp
-
-extern "C" int dsp_probe_gather(int64_t rows, int row_floats, int64_t n, int reps, float *ms_out, double *gbs_out) {
-  DSP_TRY_ARG(rows >= 1 && rows <= INT32_MAX && row_floats >= 4 && row_floats % 4 == 0 && n >= 1 && reps >= 1 &&
-                  ms_out && gbs_out,
-              "dsp_probe_gather: bad argument");
-  float4 *buf = nullptr;
-  int32_t *idx = nullptr;
-  float *sink = nullptr;
-  const size_t bytes = (size_t)rows * (size_t)row_floats * sizeof(float);
-  cudaError_t e = cudaMalloc(&buf, bytes);
-  if (e == cudaSuccess) e = cudaMalloc(&idx, sizeof(int32_t) * (size_t)n);
-  if (e == cudaSuccess) e = cudaMalloc(&sink, sizeof(float));
-  cudaEvent_t e0 = nullptr, e1 = nullptr;
-  if (e == cudaSuccess) e = cudaMemset(buf, 0, bytes);
-  if (e == cudaSuccess) e = cudaEventCreate(&e0);
-  if (e == cudaSuccess) e = cudaEventCreate(&e1);
-  if (e == cudaSuccess) {
-    dsp::probe_fill_kernel<<<148 * 8, 256>>>(idx, n, rows, 0x9E0BEull);
-    const int vpr = row_floats / 4;
-    const unsigned blocks = 148 * 8;
-    dsp::probe_gather_kernel<<<blocks, 256>>>(buf, idx, n, vpr, sink);  // warm-up
-    cudaEventRecord(e0);
-    for (int r = 0; r < reps; ++r) dsp::probe_gather_kernel<<<blocks, 256>>>(buf, idx, n, vpr, sink);
-    cudaEventRecord(e1);
-    e = cudaEventSynchronize(e1);
-    float ms = 0.f;
-    if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, e0, e1);
-    *ms_out = ms / (float)reps;
-    *gbs_out = (double)n * row_floats * sizeof(float) / ((double)*ms_out * 1e-3) / 1e9;
-  }
-  if (e0) cudaEventDestroy(e0);
-  if (e1) cudaEventDestroy(e1);
-  cudaFree(buf);
-  cudaFree(idx);
-  cudaFree(sink);
-  return e == cudaSuccess ? DSP_OK : dsp::fail(DSP_ERR_CUDA, "dsp_probe_gather: %s", cudaGetErrorString(e));
-}

@@ -326,13 +326,6 @@ int dsp_rank_check_error(dsp_rank *r);
  * records code 3 and returns. Returns DSP_ERR_TIMEOUT with *code_out = 3 when the wait gave
  * up as designed, DSP_OK if it (impossibly) completed. No fault, no hang. */
 int dsp_selftest_bounded_wait(long long budget_cycles, int *code_out);
-
-/* Gather-bandwidth probe on the current device (no counterpart in the reference): reads n
- * random rows of a rows x row_floats fp32 buffer (one warp per row, float4 loads, 8 rows in
- * flight per warp), reps times; *ms_out = mean time per pass, *gbs_out = gathered GB/s.
- * This is the ceiling of a gather-per-nonzero SpMM whose B has `rows` rows of that width.
- * Allocates its own buffers. */
-int dsp_probe_gather(int64_t rows, int row_floats, int64_t n, int reps, float *ms_out, double *gbs_out);
 /* Copy C (m_local x dims) to host. */
 int dsp_rank_download_c(dsp_rank *r, float *C_host, void *stream);
 /* Device time (ms) of the SpMM kernels of the last step, from CUDA events on the compute

@@ -1,6 +1,7 @@
 """Multi-rank pipeline parity on the GPU(s) available: P ranks in one process (sharing a
 GPU when there is only one), each fetching remote B rows from its peers' buffers and
-accumulating segment by segment; the gathered C must match the oracle. Remote rows are
+writing each C row once, in the phase after the last fetch it depends on; the gathered C
+must match the oracle. Remote rows are
 poisoned with NaN before the step, so a row that was not fetched (or fetched after its
 use) makes C non-finite instead of passing silently."""
 import os
