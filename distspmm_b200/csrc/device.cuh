@@ -44,14 +44,16 @@ struct SpmmArgs {
 };
 
 struct SpmmShape {
-  int W;           // floats per vector (4 or 1)
+  int W;           // floats per vector (8, 4 or 1)
   int LPR;         // lanes per item / chunk
   int VPL;         // vectors per lane
   int chunk_cols;  // columns per blockIdx.y
   int chunks;
 };
 
-SpmmShape spmm_shape(int N, int variant, const float *B, int64_t ldb, const float *C, int64_t ldc);
+// max_w caps the vector width for kernels instantiated only up to float4.
+SpmmShape spmm_shape(int N, int variant, const float *B, int64_t ldb, const float *C, int64_t ldc,
+                     int max_w = 8);
 int launch_spmm(const SpmmArgs &a, bool accumulate, cudaStream_t stream);
 int launch_fill_dense(float *B, int64_t row0, int64_t rows, int64_t ld, int64_t ncols, uint64_t seed,
                       cudaStream_t stream);

@@ -65,6 +65,53 @@ struct Vec<4> {
     acc.w += b.w;
   }
 };
+// 256-bit vectors (sm_100 ld/st .v8.f32): with 4 lanes per row one warp instruction reads
+// eight whole 128-byte lines of B, twice the bytes per L1 wavefront of the float4 path.
+struct Float8 {
+  float4 lo, hi;
+};
+template <>
+struct Vec<8> {
+  using T = Float8;
+  static __device__ __forceinline__ T zero() {
+    return {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
+  }
+  static __device__ __forceinline__ T ldg(const float *p, uint64_t pol) {
+    T v;
+    asm("ld.global.nc.L2::cache_hint.v8.f32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8], %9;"
+        : "=f"(v.lo.x), "=f"(v.lo.y), "=f"(v.lo.z), "=f"(v.lo.w), "=f"(v.hi.x), "=f"(v.hi.y), "=f"(v.hi.z),
+          "=f"(v.hi.w)
+        : "l"(p), "l"(pol));
+    return v;
+  }
+  static __device__ __forceinline__ T ld(const float *p) {
+    T v;
+    asm volatile("ld.global.v8.f32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=f"(v.lo.x), "=f"(v.lo.y), "=f"(v.lo.z), "=f"(v.lo.w), "=f"(v.hi.x), "=f"(v.hi.y),
+                   "=f"(v.hi.z), "=f"(v.hi.w)
+                 : "l"(p)
+                 : "memory");
+    return v;
+  }
+  static __device__ __forceinline__ void st(float *p, T v) {
+    asm volatile("st.global.v8.f32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "f"(v.lo.x), "f"(v.lo.y),
+                 "f"(v.lo.z), "f"(v.lo.w), "f"(v.hi.x), "f"(v.hi.y), "f"(v.hi.z), "f"(v.hi.w)
+                 : "memory");
+  }
+  static __device__ __forceinline__ void st_stream(float *p, T v) {
+    asm volatile("st.global.cs.v8.f32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "f"(v.lo.x), "f"(v.lo.y),
+                 "f"(v.lo.z), "f"(v.lo.w), "f"(v.hi.x), "f"(v.hi.y), "f"(v.hi.z), "f"(v.hi.w)
+                 : "memory");
+  }
+  static __device__ __forceinline__ void fma(T &acc, float s, T b) {
+    Vec<4>::fma(acc.lo, s, b.lo);
+    Vec<4>::fma(acc.hi, s, b.hi);
+  }
+  static __device__ __forceinline__ void add(T &acc, T b) {
+    Vec<4>::add(acc.lo, b.lo);
+    Vec<4>::add(acc.hi, b.hi);
+  }
+};
 template <>
 struct Vec<1> {
   using T = float;
@@ -88,11 +135,13 @@ __device__ __forceinline__ unsigned group_mask() {
   return LPR == 32 ? 0xffffffffu : (((1u << LPR) - 1u) << ((threadIdx.x & 31) & ~(LPR - 1)));
 }
 
-// nonzeros whose B vectors are loaded before their FMAs: about 8 vectors in flight per
-// lane (never more nonzeros than one shuffle round holds)
-template <int LPR, int VPL>
+// nonzeros whose B vectors are loaded before their FMAs: about 8 vectors (4 of 256 bits)
+// in flight per lane, never more nonzeros than one shuffle round holds
+template <int LPR, int VPL, int W>
 __host__ __device__ constexpr int loads_in_flight() {
-  return (8 / VPL < 1 ? 1 : 8 / VPL) < LPR ? (8 / VPL < 1 ? 1 : 8 / VPL) : LPR;
+  const int per_nonzero = (W == 8 ? 4 : 8) / VPL;
+  const int u = per_nonzero < 1 ? 1 : per_nonzero;
+  return u < LPR ? u : LPR;
 }
 
 // (column, value[, row]) entries each lane loads per round: one round covers up to 32
@@ -151,7 +200,7 @@ template <int LPR, int VPL, int W, bool kAccum>
 __global__ void __launch_bounds__(kSpmmThreads) spmm_rows_kernel(const SpmmArgs a) {
   using V = Vec<W>;
   using T = typename V::T;
-  constexpr int U = loads_in_flight<LPR, VPL>();
+  constexpr int U = loads_in_flight<LPR, VPL, W>();
   const int lane = threadIdx.x & (LPR - 1);
   const int64_t item = ((int64_t)blockIdx.x * kSpmmThreads + threadIdx.x) / LPR;
   if (item >= a.n_items) return;
@@ -212,7 +261,7 @@ template <int LPR, int VPL, int W, bool kAccum>
 __global__ void __launch_bounds__(kSpmmThreads) spmm_nnz_kernel(const SpmmArgs a) {
   using V = Vec<W>;
   using T = typename V::T;
-  constexpr int U = loads_in_flight<LPR, VPL>();
+  constexpr int U = loads_in_flight<LPR, VPL, W>();
   const int lane = threadIdx.x & (LPR - 1);
   const int64_t chunk = ((int64_t)blockIdx.x * kSpmmThreads + threadIdx.x) / LPR;
   if (chunk >= a.n_chunks) return;
@@ -343,10 +392,16 @@ using KernelFn = void (*)(const SpmmArgs);
   X(1, 1) X(2, 1) X(4, 1) X(8, 1) X(16, 1) X(32, 1) X(4, 2) X(8, 2) X(16, 2) X(32, 2) X(2, 4) X(4, 4) X(8, 4) \
   X(16, 4) X(32, 4) X(2, 8) X(4, 8) X(8, 8) X(16, 8) X(32, 8)
 #define DSP_SHAPES_W1(X) X(32, 1) X(32, 2) X(32, 4)
+// 256-bit path: the same per-lane register budgets (8-64 floats) in half the vectors
+#define DSP_SHAPES_W8(X) \
+  X(1, 1) X(2, 1) X(4, 1) X(8, 1) X(16, 1) X(32, 1) X(2, 2) X(4, 2) X(8, 2) X(16, 2) X(32, 2) X(2, 4) X(4, 4) \
+  X(8, 4) X(16, 4) X(32, 4)
 
 bool shape_supported(int W, int LPR, int VPL) {
 #define DSP_HAS(L, P) if (LPR == L && VPL == P) return true;
-  if (W == 4) {
+  if (W == 8) {
+    DSP_SHAPES_W8(DSP_HAS)
+  } else if (W == 4) {
     DSP_SHAPES_W4(DSP_HAS)
   } else {
     DSP_SHAPES_W1(DSP_HAS)
@@ -360,7 +415,9 @@ KernelFn kernel_for(int LPR, int VPL) {
 #define DSP_K(L, P)                                                                                   \
   if (LPR == L && VPL == P)                                                                            \
     return V == kRowSplit ? (KernelFn)spmm_rows_kernel<L, P, W, kAccum> : (KernelFn)spmm_nnz_kernel<L, P, W, kAccum>;
-  if (W == 4) {
+  if constexpr (W == 8) {
+    DSP_SHAPES_W8(DSP_K)
+  } else if constexpr (W == 4) {
     DSP_SHAPES_W4(DSP_K)
   } else {
     DSP_SHAPES_W1(DSP_K)
@@ -369,43 +426,57 @@ KernelFn kernel_for(int LPR, int VPL) {
   return nullptr;
 }
 
-KernelFn select_kernel(int variant, int W, bool accum, int LPR, int VPL) {
-  if (variant == kRowSplit) {
-    if (W == 4) return accum ? kernel_for<kRowSplit, 4, true>(LPR, VPL) : kernel_for<kRowSplit, 4, false>(LPR, VPL);
-    return accum ? kernel_for<kRowSplit, 1, true>(LPR, VPL) : kernel_for<kRowSplit, 1, false>(LPR, VPL);
-  }
-  if (W == 4) return accum ? kernel_for<kNnzSplit, 4, true>(LPR, VPL) : kernel_for<kNnzSplit, 4, false>(LPR, VPL);
-  return accum ? kernel_for<kNnzSplit, 1, true>(LPR, VPL) : kernel_for<kNnzSplit, 1, false>(LPR, VPL);
+template <int V>
+KernelFn select_width(int W, bool accum, int LPR, int VPL) {
+  if (W == 8) return accum ? kernel_for<V, 8, true>(LPR, VPL) : kernel_for<V, 8, false>(LPR, VPL);
+  if (W == 4) return accum ? kernel_for<V, 4, true>(LPR, VPL) : kernel_for<V, 4, false>(LPR, VPL);
+  return accum ? kernel_for<V, 1, true>(LPR, VPL) : kernel_for<V, 1, false>(LPR, VPL);
 }
 
-bool aligned16(const void *p) { return ((uintptr_t)p & 15u) == 0; }
+KernelFn select_kernel(int variant, int W, bool accum, int LPR, int VPL) {
+  return variant == kRowSplit ? select_width<kRowSplit>(W, accum, LPR, VPL)
+                              : select_width<kNnzSplit>(W, accum, LPR, VPL);
+}
+
+bool aligned(const void *p, uintptr_t bytes) { return ((uintptr_t)p & (bytes - 1)) == 0; }
 
 }  // namespace
 
-SpmmShape spmm_shape(int N, int variant, const float *B, int64_t ldb, const float *C, int64_t ldc) {
+SpmmShape spmm_shape(int N, int variant, const float *B, int64_t ldb, const float *C, int64_t ldc, int max_w) {
+  // Tuning knobs for sweeps: DSP_SPMM_VEC caps the vector width (4 keeps the float4
+  // path), DSP_SPMM_LPR forces the lanes per row.
+  static const int env_vec = [] {
+    const char *e = getenv("DSP_SPMM_VEC");
+    return e ? atoi(e) : 8;
+  }();
+  static const int forced_lpr = [] {
+    const char *e = getenv("DSP_SPMM_LPR");
+    return e ? atoi(e) : 0;
+  }();
+  const int cap = max_w < env_vec ? max_w : env_vec;
+  auto fits = [&](int w, uintptr_t bytes) {
+    return N % w == 0 && ldb % w == 0 && ldc % w == 0 && aligned(B, bytes) && aligned(C, bytes);
+  };
   SpmmShape s;
-  const bool vec4 = N % 4 == 0 && ldb % 4 == 0 && ldc % 4 == 0 && aligned16(B) && aligned16(C);
-  s.W = vec4 ? 4 : 1;
+  s.W = cap >= 8 && fits(8, 32) ? 8 : cap >= 4 && fits(4, 16) ? 4 : 1;
   const int nv = (N + s.W - 1) / s.W;  // vectors per row
-  if (vec4) {
+  if (s.W > 1) {
     // Each nonzero costs its group a few shuffles, an address and a row check no matter
-    // how many lanes share the row, so a row gets few lanes holding several float4 each
-    // (one warp then advances several rows per instruction). Measured on B200:
-    //   nnz-split: 8 vectors per lane, at most 8 lanes (N = 128 -> 4 x 8; N >= 256 -> 8 x 8
-    //              with column chunks on blockIdx.y beyond 256 columns);
-    //   row-split: 4 vectors per lane, up to 32 lanes (N = 128 -> 8 x 4).
-    static const int forced_lpr = [] {
-      const char *e = getenv("DSP_SPMM_LPR");
-      return e ? atoi(e) : 0;
-    }();
-    const int per_lane = variant == kNnzSplit ? 8 : 4;
+    // how many lanes share the row, so a row gets few lanes holding several vectors each
+    // (one warp then advances several rows per instruction). Per-lane budgets measured on
+    // B200, in floats of the output row:
+    //   nnz-split: 32 floats per lane, 2-8 lanes (N = 128 -> 4 lanes x 4 float8, or
+    //              4 x 8 float4; wider rows take column chunks on blockIdx.y);
+    //   row-split: 16 floats per lane, up to 32 lanes (N = 128 -> 8 x 2 float8 / 8 x 4 float4).
+    const int per_lane = (variant == kNnzSplit ? 32 : 16) / s.W;
     const int max_lpr = variant == kNnzSplit ? 8 : 32;
+    const int max_vpl = 32 / s.W;
     int lpr = variant == kNnzSplit ? 2 : 1;
     while (lpr * per_lane < nv && lpr < max_lpr) lpr <<= 1;
     if (forced_lpr > 0) lpr = forced_lpr;
     int vpl = 1;
-    while (lpr * vpl < nv && vpl < 8) vpl <<= 1;
-    if (!shape_supported(4, lpr, vpl)) {  // out-of-table request: one warp per row
+    while (lpr * vpl < nv && vpl < max_vpl) vpl <<= 1;
+    if (!shape_supported(s.W, lpr, vpl)) {  // out-of-table request: one warp per row
       lpr = nv <= 32 ? 1 : 32;
       while (lpr < nv && lpr < 32) lpr <<= 1;
       vpl = nv <= 32 ? 1 : nv <= 64 ? 2 : 4;
@@ -439,7 +510,7 @@ int launch_spmm(const SpmmArgs &a, bool accumulate, cudaStream_t stream) {
     if (e != cudaSuccess) return fail(DSP_ERR_CUDA, "spmm zero fill: %s", cudaGetErrorString(e));
   }
   if (a.n_split > 0) {
-    KernelFn f = s.W == 4 ? (accumulate ? spmm_fixup_kernel<4, true> : spmm_fixup_kernel<4, false>)
+    KernelFn f = s.W >= 4 ? (accumulate ? spmm_fixup_kernel<4, true> : spmm_fixup_kernel<4, false>)
                           : (accumulate ? spmm_fixup_kernel<1, true> : spmm_fixup_kernel<1, false>);
     const int64_t gx = (a.n_split * 32 + kSpmmThreads - 1) / kSpmmThreads;
     f<<<(unsigned)gx, kSpmmThreads, 0, stream>>>(a);
@@ -737,7 +808,7 @@ __global__ void __launch_bounds__(kSpmmThreads) spmm_csr_chunks_kernel(const Csr
   using V = Vec<W>;
   using T = typename V::T;
   const SpmmArgs &a = ca.base;
-  constexpr int U = loads_in_flight<LPR, VPL>();
+  constexpr int U = loads_in_flight<LPR, VPL, W>();
   constexpr int K = entries_per_lane<LPR>();
   const int lane = threadIdx.x & (LPR - 1);
   const int64_t chunk = ((int64_t)blockIdx.x * kSpmmThreads + threadIdx.x) / LPR;
@@ -840,12 +911,12 @@ namespace {
 
 using CsrKernelFn = void (*)(const CsrChunkArgs);
 
-// Every shape spmm_shape() can return.
+// Every shape spmm_shape(..., max_w = 4) can return.
 template <int W, bool kAccum>
 CsrKernelFn csr_kernel_for(int LPR, int VPL) {
 #define DSP_CK(L, P) \
   if (LPR == L && VPL == P) return spmm_csr_chunks_kernel<L, P, W, kAccum>;
-  if (W == 4) {
+  if constexpr (W == 4) {
     DSP_SHAPES_W4(DSP_CK)
   } else {
     DSP_SHAPES_W1(DSP_CK)
@@ -919,7 +990,7 @@ extern "C" int dsp_spmm_csr_f32_noalloc(const int64_t *indptr, const int64_t *in
   ca.indptr = indptr;
   ca.indices = indices;
   ca.rows = rows;
-  const SpmmShape s = spmm_shape(N, kNnzSplit, B, ldb, C, ldc);
+  const SpmmShape s = spmm_shape(N, kNnzSplit, B, ldb, C, ldc, 4);
   CsrKernelFn k = nullptr;
   if (s.W == 4)
     k = accumulate ? csr_kernel_for<4, true>(s.LPR, s.VPL) : csr_kernel_for<4, false>(s.LPR, s.VPL);

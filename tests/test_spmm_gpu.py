@@ -112,6 +112,26 @@ def test_strided_and_unaligned_operands(gpu, rmat13, variant):
 
 
 @pytest.mark.parametrize("variant", VARIANTS)
+@pytest.mark.parametrize("N", [64, 128, 256, 512])
+@pytest.mark.parametrize("pad,offset", [(4, 0), (8, 4), (0, 0)])
+def test_vector_widths(gpu, rmat13, variant, N, pad, offset):
+    """256-bit vectors need ld % 8 == 0 and 32-byte aligned rows; windows with ld % 8 == 4
+    or a 16-byte offset take the float4 kernels instead. All three agree with the oracle."""
+    import torch
+    from distspmm_b200.spmm import SpmmPlan
+    ld = N + pad
+    Bw = d.dense_b(rmat13.num_cols, ld, seed=6)
+    plan = SpmmPlan(rmat13, 0, N, variant)
+    Bt = torch.from_numpy(Bw).cuda()
+    Cw = torch.full((rmat13.num_rows, ld), 7.0, device="cuda")
+    plan(Bt[:, offset:offset + N], Cw[:, offset:offset + N])
+    torch.cuda.synchronize()
+    C = Cw.cpu().numpy()
+    assert (C[:, :offset] == 7).all() and (C[:, offset + N:] == 7).all()
+    _check(rmat13, np.ascontiguousarray(Bw[:, offset:offset + N]), C[:, offset:offset + N])
+
+
+@pytest.mark.parametrize("variant", VARIANTS)
 def test_edge_cases(gpu, variant):
     import torch
     from distspmm_b200.spmm import SpmmPlan
