@@ -655,7 +655,7 @@ void prefer_l1_carveout() {
   cudaGetDevice(&dev);
   if (dev < 31 && (done_mask >> dev) & 1) return;
   for (int v = 0; v < 2; ++v)
-    for (int w : {4, 1})
+    for (int w : {8, 4, 1})
       for (int acc = 0; acc < 2; ++acc)
         for (int lpr = 1; lpr <= 32; lpr <<= 1)
           for (int vpl = 1; vpl <= 8; vpl <<= 1)
