@@ -59,6 +59,10 @@ def parse_args(argv=None):
     ap.add_argument("--n-rolls", type=int, default=4)
     ap.add_argument("--task-dist", type=int, default=2)
     ap.add_argument("--comm-type", type=int, default=2)
+    ap.add_argument("--partition", choices=["rows", "balanced"], default="balanced",
+                    help="A rows per rank: the reference's equal-row split or work-balanced (nnz + rows)")
+    ap.add_argument("--fetch-scope", choices=["node", "rank"], default="rank",
+                    help="remote B rows fetched: the node union of all ranks' needs (reference) or this rank's own")
     ap.add_argument("--seed", type=int, default=1)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -102,6 +106,7 @@ def config_of(a, world, nnz, M):
     return {"workload": workload_name(a), "matrix": matrix_desc(a),
             "rows": M, "nnz": nnz, "dims": a.dims, "n_rolls": a.n_rolls, "task_dist": a.task_dist,
             "comm_type": a.comm_type, "parallelism": f"row1d_p{world}", "seed": a.seed,
+            "partition": a.partition if world > 1 else "single rank", "fetch_scope": a.fetch_scope,
             "l2": "flushed between steps (512 MiB write)" if not a.no_flush else "not flushed",
             "b": "U(-1,1) fp32 row-major"}
 
@@ -293,14 +298,15 @@ def main(argv=None):
     # every rank builds the whole matrix (the reference: every rank reads the whole file)
     A = make_workload(a)
     M, nnz = A.num_rows, A.nnz
-    lb, ub = planner.partition_bounds(M, world, rank)
+    lb, ub = planner.bounds(A, world, rank, a.partition)
     local = planner.partition(A, lb, ub)
     if comm is None:
         tiling = planner.tile(local, a.n_rolls)
         plan = global_plan([tiling], a.task_dist, a.n_rolls)
     else:
         tiling, plan = distributed_plan(comm, local, a.n_rolls, a.task_dist)
-    R = make_rank(local, rank, world, local_rank, a.dims, M, lb, tiling, plan, a.comm_type, "h100", 4)
+    R = make_rank(local, rank, world, local_rank, a.dims, M, lb, tiling, plan, a.comm_type, "h100", 4,
+                  fetch_scope=a.fetch_scope)
     if comm is not None:
         connect_peers(comm, R)
     st = R.stats()

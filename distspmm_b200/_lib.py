@@ -95,6 +95,7 @@ PROTOTYPES = {
     "dsp_gen_uniform": (c_int, [c_i64, c_i64, c_u64, P(dsp_csr)]),
     "dsp_fill_dense_host": (c_int, [P(c_f32), c_i64, c_i64, c_i64, c_i64, c_u64]),
     "dsp_partition_bounds": (c_int, [c_i64, c_int, c_int, P(c_i64), P(c_i64)]),
+    "dsp_partition_bounds_balanced": (c_int, [P(c_i64), c_i64, c_int, c_int, P(c_i64), P(c_i64)]),
     "dsp_partition": (c_int, [P(dsp_csr), c_i64, c_i64, P(dsp_csr)]),
     "dsp_tile_counts": (c_int, [P(dsp_csr), c_int, P(c_i64), P(c_i32), P(c_i32), P(c_i64)]),
     "dsp_tile_needed": (c_int, [P(dsp_csr), c_int, P(c_i64), P(c_i32)]),

@@ -241,6 +241,34 @@ extern "C" int dsp_partition_bounds(int64_t M, int P, int rank, int64_t *lb, int
   return DSP_OK;
 }
 
+// Contiguous rows with equal work: cost(rows [0, i)) = indptr[i] + i (one B-row gather per
+// nonzero, one C-row write per row); rank p starts at the first row whose prefix cost
+// reaches p/P of the total. Boundaries are monotone in p, so the P ranges tile [0, M).
+extern "C" int dsp_partition_bounds_balanced(const int64_t *indptr, int64_t M, int P, int rank, int64_t *lb,
+                                             int64_t *ub) {
+  DSP_TRY_ARG(indptr && lb && ub && P > 0 && rank >= 0 && rank < P && M >= 0,
+              "dsp_partition_bounds_balanced: bad argument");
+  const int64_t total = indptr[M] - indptr[0] + M;
+  auto start = [&](int p) -> int64_t {
+    if (p <= 0) return 0;
+    if (p >= P) return M;
+    // target = ceil(total * p / P) without overflow for totals below 2^62 / P
+    const int64_t target = (int64_t)(((__int128)total * p + P - 1) / P);
+    int64_t lo = 0, hi = M;  // first i in [0, M] with cost(i) >= target
+    while (lo < hi) {
+      const int64_t mid = lo + (hi - lo) / 2;
+      if (indptr[mid] - indptr[0] + mid >= target)
+        hi = mid;
+      else
+        lo = mid + 1;
+    }
+    return lo;
+  };
+  *lb = start(rank);
+  *ub = start(rank + 1);
+  return DSP_OK;
+}
+
 extern "C" int dsp_partition(const dsp_csr *g, int64_t lb, int64_t ub, dsp_csr *local) {
   DSP_TRY_ARG(g && local && g->indptr, "dsp_partition: null argument");
   if (lb < 0 || ub > g->num_rows || lb > ub)

@@ -59,12 +59,20 @@ extern "C" int dsp_run(const dsp_args *A, dsp_report *rep) {
   rep->nnz = g->nnz;
   rep->T = T;
 
+  // Extensions beyond the reference's pipeline, off by default: DSP_PARTITION=balanced
+  // (work-balanced rows instead of equal rows) and DSP_FETCH_SCOPE=rank (each rank fetches
+  // its own needed rows instead of the node union).
+  const char *part_env = getenv("DSP_PARTITION"), *scope_env = getenv("DSP_FETCH_SCOPE");
+  const bool balanced = part_env && strcmp(part_env, "balanced") == 0;
+  const bool per_rank = scope_env && strcmp(scope_env, "rank") == 0;
+
   // 2. 1-D row partition (src/dist_spmm_node.cu:82-99)
   t0 = now_ms();
   std::vector<CsrHolder> local((size_t)P);
   std::vector<int64_t> lb((size_t)P), ub((size_t)P);
   for (int p = 0; p < P; ++p) {
-    if ((rc = dsp_partition_bounds(M, P, p, &lb[(size_t)p], &ub[(size_t)p])) ||
+    if ((rc = balanced ? dsp_partition_bounds_balanced(g->indptr, M, P, p, &lb[(size_t)p], &ub[(size_t)p])
+                       : dsp_partition_bounds(M, P, p, &lb[(size_t)p], &ub[(size_t)p])) ||
         (rc = dsp_partition(g, lb[(size_t)p], ub[(size_t)p], &local[(size_t)p].m)))
       return rc;
   }
@@ -125,7 +133,8 @@ extern "C" int dsp_run(const dsp_args *A, dsp_report *rep) {
   double t_sel = 0;
   for (int p = 0; p < P; ++p) {
     double s0 = now_ms();
-    if ((rc = dsp_comm_select(A->comm_type, dims, &intra, &inter, T, mcount.data(), &n_slice[(size_t)p * T],
+    const int32_t *counts = per_rank ? &n_col[(size_t)p * T] : mcount.data();
+    if ((rc = dsp_comm_select(A->comm_type, dims, &intra, &inter, T, counts, &n_slice[(size_t)p * T],
                               sparse[(size_t)p].data(), nullptr)))
       return rc;
     t_sel += now_ms() - s0;
@@ -142,8 +151,8 @@ extern "C" int dsp_run(const dsp_args *A, dsp_report *rep) {
     d.local = &local[(size_t)p].m;
     d.remap = remap.data();
     d.sparse = sparse[(size_t)p].data();
-    d.needed_offsets = moff.data();
-    d.needed_cols = merged.data();
+    d.needed_offsets = per_rank ? off[(size_t)p].data() : moff.data();
+    d.needed_cols = per_rank ? need[(size_t)p].data() : merged.data();
     d.n_slice = &n_slice[(size_t)p * T];
     if ((rc = dsp_rank_create(&d, &ranks[(size_t)p].r))) return rc;
     if (A->b_ones) {
@@ -188,7 +197,8 @@ extern "C" int dsp_run(const dsp_args *A, dsp_report *rep) {
   // traffic counters (src/dist_spmm_node.cu:401-406), summed over ranks
   for (int p = 0; p < P; ++p) {
     int64_t b = 0;
-    dsp_traffic_intra(p, T, remap.data(), sparse[(size_t)p].data(), mcount.data(), &n_slice[(size_t)p * T], dims, &b);
+    dsp_traffic_intra(p, T, remap.data(), sparse[(size_t)p].data(), per_rank ? &n_col[(size_t)p * T] : mcount.data(),
+                      &n_slice[(size_t)p * T], dims, &b);
     rep->traffic_intra += b;
     dsp_rank_stats st;
     dsp_rank_stats_get(ranks[(size_t)p].r, &st);

@@ -12,7 +12,7 @@ is how the multi-rank path is exercised on a single GPU.
 from __future__ import annotations
 
 import ctypes
-from dataclasses import dataclass, field
+from dataclasses import dataclass, field, replace
 
 import numpy as np
 
@@ -166,14 +166,33 @@ class Rank:
             pass
 
 
+FETCH_SCOPES = ("node", "rank")
+
+
+def fetch_view(plan: GlobalPlan, tiling, scope: str = "node") -> GlobalPlan:
+    """The needed lists a rank fetches from: the node-merged union of every rank's lists
+    ("node", the reference's double_level_comm_node_processing, src/utils.h:439-547), or
+    only this rank's own lists ("rank": fewer NVLink bytes when the ranks' needs differ;
+    the selector then sees this rank's own list sizes)."""
+    if scope == "node":
+        return plan
+    if scope == "rank":
+        return replace(plan, n_col=np.ascontiguousarray(tiling.n_col, np.int32),
+                       offsets=np.ascontiguousarray(tiling.offsets, np.int64),
+                       merged=np.ascontiguousarray(tiling.needed, np.int32))
+    raise ValueError(f"fetch scope {scope!r}: expected one of {FETCH_SCOPES}")
+
+
 def make_rank(local: Csr, rank: int, world: int, device: int, dims: int, M: int, m_lb: int, tiling,
               plan: GlobalPlan, comm_type: int, platform: str = "h100", n_streams: int = 4,
-              fetch_engine: str = "lsu") -> Rank:
+              fetch_engine: str = "lsu", fetch_scope: str = "node") -> Rank:
     """Selector (CommMan_hp ctor, src/comm_man.h:341-410) + rank construction."""
-    sparse = planner.comm_select(comm_type, dims, plan.n_col, tiling.n_slice, platform)
-    r = Rank(local, rank, world, device, dims, M, m_lb, plan, tiling.n_slice, sparse, n_streams, fetch_engine)
+    view = fetch_view(plan, tiling, fetch_scope)
+    sparse = planner.comm_select(comm_type, dims, view.n_col, tiling.n_slice, platform)
+    r = Rank(local, rank, world, device, dims, M, m_lb, view, tiling.n_slice, sparse, n_streams, fetch_engine)
     r.sparse = sparse
     r.n_slice = tiling.n_slice
+    r.n_col = view.n_col
     return r
 
 
@@ -202,23 +221,24 @@ class LocalGroup:
 
 def build_local_group(g: Csr, world: int, devices, dims: int, n_rolls: int = 4, task_dist: int = 2,
                       comm_type: int = 2, platform: str = "h100", n_streams: int = 4,
-                      fetch_engine: str = "lsu") -> LocalGroup:
+                      fetch_engine: str = "lsu", partition: str = "rows",
+                      fetch_scope: str = "node") -> LocalGroup:
     """All `world` ranks of the pipeline in this process; devices[p] is rank p's GPU
     (ranks may share one). Peers read each other's B directly (same device, or peer
     access between devices)."""
     M = g.num_rows
     T = world * n_rolls
-    bounds = [planner.partition_bounds(M, world, p) for p in range(world)]
+    bounds = [planner.bounds(g, world, p, partition) for p in range(world)]
     locals_ = [planner.partition(g, lb, ub) for lb, ub in bounds]
     tilings = [planner.tile(loc, T) for loc in locals_]
     plan = global_plan(tilings, task_dist, n_rolls)
     ranks = [make_rank(locals_[p], p, world, devices[p], dims, M, bounds[p][0], tilings[p], plan, comm_type,
-                       platform, n_streams, fetch_engine) for p in range(world)]
+                       platform, n_streams, fetch_engine, fetch_scope) for p in range(world)]
     for p in range(world):
         for q in range(world):
             if p != q:
                 ranks[p].set_peer(q, ranks[q].b_ptr(), devices[q])
-    traffic = sum(planner.traffic_intra(p, plan.remap, ranks[p].sparse, plan.n_col, tilings[p].n_slice, dims)
+    traffic = sum(planner.traffic_intra(p, plan.remap, ranks[p].sparse, ranks[p].n_col, tilings[p].n_slice, dims)
                   for p in range(world))
     return LocalGroup(ranks, plan, bounds, tilings, dims, M, g.nnz, traffic, [r.sparse for r in ranks])
 

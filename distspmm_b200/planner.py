@@ -37,6 +37,29 @@ def partition_bounds(M: int, P_: int, rank: int):
     return lb.value, ub.value
 
 
+def partition_bounds_balanced(indptr: np.ndarray, P_: int, rank: int):
+    """Contiguous rows of equal cost (nonzeros + rows); not in the reference (an addition
+    for skewed graphs, where the equal-row split of partition_bounds overloads rank 0)."""
+    ip = np.ascontiguousarray(indptr, np.int64)
+    lb, ub = c_i64(), c_i64()
+    call("dsp_partition_bounds_balanced", _ptr(ip, c_i64), ip.size - 1, P_, rank, ctypes.byref(lb),
+         ctypes.byref(ub))
+    return lb.value, ub.value
+
+
+PARTITIONS = ("rows", "balanced")
+
+
+def bounds(g: Csr, P_: int, rank: int, how: str = "rows"):
+    """Row range of `rank`: the reference's equal-row split ("rows") or the work-balanced
+    one ("balanced")."""
+    if how == "rows":
+        return partition_bounds(g.num_rows, P_, rank)
+    if how == "balanced":
+        return partition_bounds_balanced(g.indptr, P_, rank)
+    raise ValueError(f"partition {how!r}: expected one of {PARTITIONS}")
+
+
 def partition(g: Csr, lb: int, ub: int) -> Csr:
     c = g.to_c()
     out = dsp_csr()

@@ -24,10 +24,12 @@ def _devices(world):
     return [p % n for p in range(world)]
 
 
-def _run_group(A, world, dims, rolls, task_dist, comm_type, seed=21, poison=True, fetch_engine="lsu"):
+def _run_group(A, world, dims, rolls, task_dist, comm_type, seed=21, poison=True, fetch_engine="lsu",
+               partition="rows", fetch_scope="node"):
     import torch
     from distspmm_b200.dist import build_local_group
-    g = build_local_group(A, world, _devices(world), dims, rolls, task_dist, comm_type, fetch_engine=fetch_engine)
+    g = build_local_group(A, world, _devices(world), dims, rolls, task_dist, comm_type, fetch_engine=fetch_engine,
+                          partition=partition, fetch_scope=fetch_scope)
     for r in g.ranks:
         if poison:
             r.poison_remote()
@@ -133,6 +135,31 @@ def test_group_upload_from_host_and_repeat(gpu, rmat12):
     g.close()
 
 
+@pytest.mark.parametrize("partition,fetch_scope", [("balanced", "node"), ("rows", "rank"), ("balanced", "rank")])
+@pytest.mark.parametrize("world,comm_type", [(2, 2), (3, 1), (4, 0), (8, 2)])
+def test_group_parity_partition_and_fetch_scope(gpu, rmat12, partition, fetch_scope, world, comm_type):
+    """Work-balanced rows and per-rank fetch lists: same C (remote rows NaN-poisoned, so a
+    row missing from a rank's own list would show), fewer fetched rows per rank."""
+    g, C = _run_group(rmat12, world, 128, 4, 2, comm_type, partition=partition, fetch_scope=fetch_scope)
+    _check(rmat12, C, 128)
+    if partition == "balanced":
+        cost = [int(rmat12.indptr[ub] - rmat12.indptr[lb]) + (ub - lb) for lb, ub in g.bounds]
+        assert max(cost) <= (rmat12.nnz + rmat12.num_rows) / world + int(np.diff(rmat12.indptr).max()) + 1
+    if fetch_scope == "rank" and comm_type == 1:  # all sparse: each rank fetches only its own rows
+        for r, t in zip(g.ranks, g.tilings):
+            remote = sum(int(t.n_col[k]) for k in range(g.plan.T)
+                         if g.plan.remap[k] != r.rank and t.nnz[k] > 0)
+            assert r.stats()["fetch_rows"] == remote
+    g.close()
+
+
+def test_group_stencil_per_rank_fetch(gpu):
+    A = d.gen_stencil27(20, seed=4)
+    g, C = _run_group(A, 4, 128, 4, 2, 2, partition="balanced", fetch_scope="rank")
+    _check(A, C, 128)
+    g.close()
+
+
 def test_dsp_run_pipeline(gpu, rmat12):
     """dsp_run: the whole dist_spmm_node program in-process, C returned to the host."""
     import ctypes
@@ -157,6 +184,51 @@ def test_dsp_run_pipeline(gpu, rmat12):
     assert rep.traffic_intra == g.traffic_intra
     assert list(rep.remap[:rep.T]) == g.plan.remap.tolist()
     g.close()
+
+
+_DSP_RUN_SNIPPET = r"""
+import ctypes, sys
+import numpy as np
+import distspmm_b200 as d, oracle
+from distspmm_b200 import _lib
+A = d.gen_rmat(12, seed=8)
+world, dims = 4, 128
+import torch
+n = torch.cuda.device_count()
+devs = (ctypes.c_int * world)(*[p % n for p in range(world)])
+C = np.zeros((A.num_rows, dims), np.float32)
+c = A.to_c()
+a = _lib.dsp_args()
+a.matrix = ctypes.pointer(c)
+a.dims, a.task_dist, a.comm_type, a.n_rolls, a.repeat, a.n_streams = dims, 2, 2, 4, 7, 4
+a.world, a.devices, a.platform, a.b_seed, a.b_ones = world, devs, 0, 21, 0
+a.c_out = C.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+rep = _lib.dsp_report()
+_lib.call("dsp_run", ctypes.byref(a), ctypes.byref(rep))
+ref, ab = oracle.spmm_f64(A.indptr, A.indices, A.values, d.dense_b(A.num_cols, dims, 21))
+ok, worst = oracle.check_close(C, ref, ab, 1e-5)
+print(int(ok and np.isfinite(C).all()), rep.traffic_intra, rep.fetched_bytes)
+"""
+
+
+def test_dsp_run_partition_and_fetch_scope_env(gpu):
+    """The CLI pipeline's opt-in extensions (DSP_PARTITION=balanced, DSP_FETCH_SCOPE=rank):
+    same C as the oracle, and no more fetched bytes than the reference-semantics run."""
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+    def run(**env):
+        e = dict(os.environ, PYTHONPATH=root, **env)
+        out = subprocess.run([os.environ.get("PYTHON", "python"), "-c", _DSP_RUN_SNIPPET], env=e, cwd=root,
+                             capture_output=True, text=True, timeout=600)
+        assert out.returncode == 0, out.stderr[-2000:]
+        ok, traffic, fetched = (int(x) for x in out.stdout.split()[-3:])
+        assert ok == 1
+        return traffic, fetched
+
+    _, f_ref = run()
+    _, f_rank = run(DSP_FETCH_SCOPE="rank")
+    assert f_rank <= f_ref
+    run(DSP_PARTITION="balanced", DSP_FETCH_SCOPE="rank")
 
 
 def test_cli_report_format(gpu, tmp_path):

@@ -133,3 +133,53 @@ def test_alloc_slice_and_random():
     r = planner.alloc_random(8, 4, seed=9)
     assert sorted(r.tolist()) == sorted(planner.alloc_slice(8, 4).tolist())
     assert (r == planner.alloc_random(8, 4, seed=9)).all()
+
+
+@pytest.mark.parametrize("P", [1, 2, 3, 8, 64])
+def test_balanced_partition_tiles_rows_with_equal_cost(rmat, P):
+    """Work-balanced bounds: contiguous, in rank order, covering [0, M); every range's cost
+    (nonzeros + rows) within one row of total / P."""
+    ip = rmat.indptr
+    M = rmat.num_rows
+    b = [planner.partition_bounds_balanced(ip, P, p) for p in range(P)]
+    assert b[0][0] == 0 and b[-1][1] == M
+    assert all(b[p][1] == b[p + 1][0] for p in range(P - 1))
+    assert all(lb <= ub for lb, ub in b)
+    cost = np.asarray(ip, np.int64) + np.arange(M + 1)
+    total = int(cost[-1])
+    worst_row = int(np.diff(cost).max())
+    for lb, ub in b:
+        assert int(cost[ub] - cost[lb]) <= -(-total // P) + worst_row
+    # the rule itself: rank p starts at the first row whose prefix cost reaches ceil(p * total / P)
+    for p in range(1, P):
+        target = -(-(total * p) // P)
+        assert b[p][0] == int(np.searchsorted(cost, target, side="left"))
+
+
+def test_balanced_partition_edge_cases():
+    ip = np.array([0], np.int64)  # no rows
+    assert planner.partition_bounds_balanced(ip, 4, 3) == (0, 0)
+    ip = np.array([0, 0, 0, 5, 5], np.int64)  # empty rows and one heavy row; more ranks than rows
+    b = [planner.partition_bounds_balanced(ip, 6, p) for p in range(6)]
+    assert b[0][0] == 0 and b[-1][1] == 4 and all(b[p][1] == b[p + 1][0] for p in range(5))
+    with pytest.raises(d.DspError):
+        planner.partition_bounds_balanced(ip, 0, 0)
+
+
+def test_fetch_view_scopes(rmat):
+    from distspmm_b200.dist import fetch_view, global_plan
+    P, rolls = 4, 2
+    bounds = [planner.partition_bounds(rmat.num_rows, P, p) for p in range(P)]
+    tilings = [planner.tile(planner.partition(rmat, lb, ub), P * rolls) for lb, ub in bounds]
+    plan = global_plan(tilings, 2, rolls)
+    assert fetch_view(plan, tilings[1], "node") is plan
+    v = fetch_view(plan, tilings[1], "rank")
+    assert np.array_equal(v.n_col, tilings[1].n_col) and np.array_equal(v.merged, tilings[1].needed)
+    assert np.array_equal(v.remap, plan.remap) and v.T == plan.T
+    # each rank's own list is a subset of the node union, tile by tile
+    for t in range(plan.T):
+        own = set(v.merged[v.offsets[t]:v.offsets[t + 1]].tolist())
+        union = set(plan.merged[plan.offsets[t]:plan.offsets[t + 1]].tolist())
+        assert own <= union
+    with pytest.raises(ValueError):
+        fetch_view(plan, tilings[1], "cluster")
