@@ -63,6 +63,9 @@ def parse_args(argv=None):
                     help="A rows per rank: the reference's equal-row split or work-balanced (nnz + rows)")
     ap.add_argument("--fetch-scope", choices=["node", "rank"], default="rank",
                     help="remote B rows fetched: the node union of all ranks' needs (reference) or this rank's own")
+    ap.add_argument("--pipeline", choices=["auto", "rows", "split"], default="auto",
+                    help="phases: whole rows after their last fetch, nonzeros per ring position, or per matrix")
+    ap.add_argument("--fetch-streams", type=int, default=4, help="concurrent fetch streams (nvlink_num_producers)")
     ap.add_argument("--seed", type=int, default=1)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -107,6 +110,7 @@ def config_of(a, world, nnz, M):
             "rows": M, "nnz": nnz, "dims": a.dims, "n_rolls": a.n_rolls, "task_dist": a.task_dist,
             "comm_type": a.comm_type, "parallelism": f"row1d_p{world}", "seed": a.seed,
             "partition": a.partition if world > 1 else "single rank", "fetch_scope": a.fetch_scope,
+            "pipeline": a.pipeline, "fetch_streams": a.fetch_streams,
             "l2": "flushed between steps (512 MiB write)" if not a.no_flush else "not flushed",
             "b": "U(-1,1) fp32 row-major"}
 
@@ -305,8 +309,8 @@ def main(argv=None):
         plan = global_plan([tiling], a.task_dist, a.n_rolls)
     else:
         tiling, plan = distributed_plan(comm, local, a.n_rolls, a.task_dist)
-    R = make_rank(local, rank, world, local_rank, a.dims, M, lb, tiling, plan, a.comm_type, "h100", 4,
-                  fetch_scope=a.fetch_scope)
+    R = make_rank(local, rank, world, local_rank, a.dims, M, lb, tiling, plan, a.comm_type, "h100", a.fetch_streams,
+                  fetch_scope=a.fetch_scope, pipeline=a.pipeline)
     if comm is not None:
         connect_peers(comm, R)
     st = R.stats()
@@ -443,7 +447,8 @@ def main(argv=None):
                      "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})"},
         "e2e": e2e, "cpu_baseline": cpu, "clocks": clk,
         "gpu_launches": a.steps * st["kernels_per_step"],
-        "nvlink": {"fetched_bytes_per_step": fetch_bytes,
+        "nvlink": {"fetched_bytes_per_step": fetch_bytes, "pipeline_rank0": ["", "rows", "split"][st["pipeline"]],
+                   "phase0_nnz_rank0": st["phase0_nnz"],
                    "max_rank_compute_ms": round(t_comp_max, 4),
                    "max_rank_compute_idle_ms": round(idle_max, 4),
                    "timeline_rank0": timeline if rank == 0 else None},

@@ -41,6 +41,10 @@ struct SpmmArgs {
   int64_t ldc;
   float *partial;  // [slots][N]
   int N;
+  // split pipeline: output row r is accumulated (C += ...) when first_phase[r] < phase,
+  // written otherwise; nullptr = every row written (or accumulated, per the launch)
+  const uint8_t *first_phase;
+  int phase;
 };
 
 struct SpmmShape {

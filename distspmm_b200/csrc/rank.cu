@@ -7,11 +7,14 @@
 //         recycled (the reference's 4-slot ring of src/dist_spmm_node.cu:199-203 with its
 //         reuse race, replaced by one full-height buffer: 180 GB HBM holds B at every
 //         configuration this engine targets).
-//   C     [m_local x dims] fp32 row-major, every row written exactly once per step.
+//   C     [m_local x dims] fp32 row-major.
 //   A     one DevOperand per phase. Peers are visited in the reference's ring order
-//         (me + k) % P (src/dist_spmm_node.cu:339-343); a local row belongs to phase k, the
-//         latest ring position among the owners of its columns, and phase k holds whole
-//         rows (all their nonzeros). Phase 0 = rows that need only tiles this rank owns.
+//         (me + k) % P (src/dist_spmm_node.cu:339-343). Rows pipeline: a local row belongs
+//         to phase k, the latest ring position among the owners of its columns, and phase
+//         k holds whole rows (all their nonzeros): every C row is written exactly once.
+//         Phase 0 = rows that need only tiles this rank owns. Split pipeline: phase k holds
+//         the nonzeros of ring position k; a row is written by its first phase and
+//         accumulated by later ones (first_phase[] on the device).
 //         Rows without nonzeros are listed apart and zero-filled.
 //   scratch: partial rows of rows cut between work units, shared by the phases (they run
 //         in order on one stream).
@@ -72,6 +75,8 @@ struct dsp_rank {
     DevOperand op;  // the rows of phase k
   };
   std::vector<Segment> segs;  // one per phase / ring position k
+  int pipeline = DSP_PIPELINE_ROWS;
+  uint8_t *d_first_phase = nullptr;  // split pipeline: first phase writing each local row
   int32_t *d_empty = nullptr;  // local rows without nonzeros (zero-filled each step)
   int64_t n_empty = 0;
 
@@ -97,30 +102,99 @@ struct dsp_rank {
 
 namespace {
 
+// Split pipeline: phase k holds the nonzeros whose column tile is owned by ring position
+// k (rows listed in ascending order, their nonzeros in column order); first[i] is the
+// first phase touching row i, where the row is written, later phases adding to it.
+int build_split_phases(dsp_rank *r, const dsp_csr *a, const std::vector<int32_t> &first) {
+  const int P = r->P, me = r->me;
+  const int64_t m = a->num_rows, nnz = a->nnz, cpt = r->cpt;
+  std::vector<uint8_t> pos((size_t)std::max<int64_t>(nnz, 1));
+  parallel_for(nnz, [&](int64_t b, int64_t e) {
+    for (int64_t j = b; j < e; ++j) pos[(size_t)j] = (uint8_t)((r->remap[(size_t)(a->indices[j] / cpt)] - me + P) % P);
+  }, 1 << 16);
+  std::vector<uint8_t> fp((size_t)std::max<int64_t>(m, 1), 0xff);
+  for (int64_t i = 0; i < m; ++i)
+    if (first[(size_t)i] >= 0) fp[(size_t)i] = (uint8_t)first[(size_t)i];
+  int rc = dev_upload(&r->d_first_phase, fp.data(), fp.size());
+  if (rc) return rc;
+  for (int k = 0; k < P; ++k) {
+    auto &S = r->segs[(size_t)k];
+    S.owner = (me + k) % P;
+    std::vector<int32_t> rows;
+    std::vector<int64_t> ptr(1, 0), idx;
+    std::vector<float> val;
+    for (int64_t i = 0; i < m; ++i) {
+      const int64_t before = (int64_t)idx.size();
+      for (int64_t j = a->indptr[i]; j < a->indptr[i + 1]; ++j)
+        if (pos[(size_t)j] == k) {
+          idx.push_back(a->indices[j]);
+          val.push_back(a->values[j]);
+        }
+      if ((int64_t)idx.size() > before) {
+        rows.push_back((int32_t)i);
+        ptr.push_back((int64_t)idx.size());
+      }
+    }
+    if (idx.empty()) {
+      idx.push_back(0);
+      val.push_back(0.f);
+    }
+    rc = S.op.upload(r->device, m, r->M, ptr.data(), rows.data(), (int64_t)rows.size(), idx.data(), val.data(), 0,
+                     ptr.back(), r->dims, false);
+    if (rc) return rc;
+    r->scratch_floats = std::max(r->scratch_floats, S.op.pieces * (int64_t)r->dims);
+  }
+  return DSP_OK;
+}
+
 // Phase of every local row: the latest ring position (owner - me mod P) among its
 // columns' tiles; -1 for rows without nonzeros. Phase k holds whole rows, so each row is
-// computed once, with all its nonzeros, after the fetches of ring positions 1..k.
-int build_phases(dsp_rank *r, const dsp_csr *a) {
+// computed once, with all its nonzeros, after the fetches of ring positions 1..k. The
+// split pipeline (chosen here for DSP_PIPELINE_AUTO when less than half of the nonzeros
+// would run before any fetch lands) cuts rows by ring position instead.
+int build_phases(dsp_rank *r, const dsp_csr *a, int pipeline) {
   const int P = r->P, me = r->me;
   const int64_t m = a->num_rows, cpt = r->cpt;
-  std::vector<int32_t> phase((size_t)std::max<int64_t>(m, 1), -1);
+  std::vector<int32_t> phase((size_t)std::max<int64_t>(m, 1), -1), first((size_t)std::max<int64_t>(m, 1), -1);
   parallel_for(m, [&](int64_t b, int64_t e) {
     for (int64_t i = b; i < e; ++i) {
-      int32_t ph = -1;
-      for (int64_t j = a->indptr[i]; j < a->indptr[i + 1]; ++j)
-        ph = std::max<int32_t>(ph, (r->remap[(size_t)(a->indices[j] / cpt)] - me + P) % P);
+      int32_t ph = -1, lo = P;
+      for (int64_t j = a->indptr[i]; j < a->indptr[i + 1]; ++j) {
+        const int32_t k = (r->remap[(size_t)(a->indices[j] / cpt)] - me + P) % P;
+        ph = std::max(ph, k);
+        lo = std::min(lo, k);
+      }
       phase[(size_t)i] = ph;
+      first[(size_t)i] = ph < 0 ? -1 : lo;
     }
   }, 1024);
   std::vector<int32_t> empty;
-  for (int64_t i = 0; i < m; ++i)
+  int64_t rows_phase0_nnz = 0;
+  for (int64_t i = 0; i < m; ++i) {
     if (phase[(size_t)i] < 0) empty.push_back((int32_t)i);
+    if (phase[(size_t)i] == 0) rows_phase0_nnz += a->indptr[i + 1] - a->indptr[i];
+  }
   r->n_empty = (int64_t)empty.size();
   if (r->n_empty) {
     int rc = dev_upload(&r->d_empty, empty.data(), sizeof(int32_t) * empty.size());
     if (rc) return rc;
   }
   r->segs.resize((size_t)P);
+  // nonzeros in tiles this rank owns: what the split pipeline computes before any fetch
+  int64_t local_nnz = 0;
+  for (int64_t j = 0; j < a->nnz; ++j) local_nnz += r->remap[(size_t)(a->indices[j] / cpt)] == me;
+  // AUTO: split only when whole rows would leave most of the work behind the fetches and
+  // the owned tiles hold enough work (>= 30 %) to hide them; measured on B200 at P = 2:
+  // R-MAT (16 % local, hub rows) runs 20 % slower split, the stencil is rows-bound.
+  if (pipeline == DSP_PIPELINE_AUTO)
+    pipeline = 2 * rows_phase0_nnz < a->nnz && 10 * local_nnz >= 3 * a->nnz ? DSP_PIPELINE_SPLIT : DSP_PIPELINE_ROWS;
+  if (P == 1 || P > 255) pipeline = DSP_PIPELINE_ROWS;
+  r->pipeline = pipeline;
+  if (pipeline == DSP_PIPELINE_SPLIT) {
+    r->stats.phase0_nnz = local_nnz;
+    return build_split_phases(r, a, first);
+  }
+  r->stats.phase0_nnz = rows_phase0_nnz;
   for (int k = 0; k < P; ++k) {
     auto &S = r->segs[(size_t)k];
     S.owner = (me + k) % P;
@@ -240,7 +314,7 @@ extern "C" int dsp_rank_create(const dsp_rank_desc *d, dsp_rank **out) {
     return bail(fail(DSP_ERR_NOMEM, "C (%zu bytes): %s", cbytes, cudaGetErrorString(e)));
   if ((e = cudaMalloc(&r->d_err, sizeof(int))) != cudaSuccess || (e = cudaMemset(r->d_err, 0, sizeof(int))) != cudaSuccess)
     return bail(fail(DSP_ERR_NOMEM, "error flag: %s", cudaGetErrorString(e)));
-  if ((rc = build_phases(r, d->local))) return bail(rc);
+  if ((rc = build_phases(r, d->local, d->pipeline))) return bail(rc);
   if (r->P > 1 && (rc = build_fetch(r, d))) return bail(rc);
   if (r->scratch_floats > 0 && (e = cudaMalloc(&r->scratch, sizeof(float) * (size_t)r->scratch_floats)) != cudaSuccess)
     return bail(fail(DSP_ERR_NOMEM, "scratch: %s", cudaGetErrorString(e)));
@@ -288,7 +362,9 @@ extern "C" int dsp_rank_create(const dsp_rank_desc *d, dsp_rank **out) {
     for (int64_t j = 0; j < r->nnz_local; ++j) seen[(size_t)d->local->indices[j]] = 1;
     for (auto x : seen) s.distinct_cols += x;
   }
-  s.device_bytes = (int64_t)bbytes + (int64_t)cbytes + r->scratch_floats * 4;
+  s.pipeline = r->pipeline;
+  s.device_bytes = (int64_t)bbytes + (int64_t)cbytes + r->scratch_floats * 4 +
+                   (r->d_first_phase ? std::max<int64_t>(r->m_local, 1) : 0);
   for (auto &S : r->segs) s.device_bytes += S.op.device_bytes();
   for (auto &F : r->fetch) s.device_bytes += F.n_rows * 4;
   *out = r;
@@ -309,6 +385,7 @@ extern "C" void dsp_rank_destroy(dsp_rank *r) {
   if (r->C) cudaFree(r->C);
   if (r->scratch) cudaFree(r->scratch);
   if (r->d_empty) cudaFree(r->d_empty);
+  if (r->d_first_phase) cudaFree(r->d_first_phase);
   if (r->d_err) cudaFree(r->d_err);
   for (auto s : r->fstreams) cudaStreamDestroy(s);
   if (r->compute) cudaStreamDestroy(r->compute);
@@ -469,7 +546,12 @@ extern "C" int dsp_rank_step(dsp_rank *r, void *stream_v) {
     for (; waited < k; ++waited)
       if (has_fetch[(size_t)waited + 1]) DSP_CUDA(cudaStreamWaitEvent(r->compute, r->ev_fetch[(size_t)waited + 1], 0));
     DSP_CUDA(cudaEventRecord(r->ev_seg_begin[(size_t)k], r->compute));
-    if ((rc = launch_spmm(op.args(r->B, r->dims, r->C, r->dims, r->dims, r->scratch), false, r->compute))) return rc;
+    SpmmArgs sa = op.args(r->B, r->dims, r->C, r->dims, r->dims, r->scratch);
+    if (r->pipeline == DSP_PIPELINE_SPLIT) {  // rows written by an earlier phase are accumulated
+      sa.first_phase = r->d_first_phase;
+      sa.phase = k;
+    }
+    if ((rc = launch_spmm(sa, false, r->compute))) return rc;
     DSP_CUDA(cudaEventRecord(r->ev_seg_end[(size_t)k], r->compute));
     r->seg_ran[(size_t)k] = true;
   }

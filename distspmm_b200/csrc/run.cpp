@@ -65,6 +65,12 @@ extern "C" int dsp_run(const dsp_args *A, dsp_report *rep) {
   const char *part_env = getenv("DSP_PARTITION"), *scope_env = getenv("DSP_FETCH_SCOPE");
   const bool balanced = part_env && strcmp(part_env, "balanced") == 0;
   const bool per_rank = scope_env && strcmp(scope_env, "rank") == 0;
+  // DSP_PIPELINE=rows|split forces the phase structure (default: chosen per rank).
+  const char *pipe_env = getenv("DSP_PIPELINE");
+  const int pipeline = !pipe_env                        ? DSP_PIPELINE_AUTO
+                       : strcmp(pipe_env, "rows") == 0  ? DSP_PIPELINE_ROWS
+                       : strcmp(pipe_env, "split") == 0 ? DSP_PIPELINE_SPLIT
+                                                        : DSP_PIPELINE_AUTO;
 
   // 2. 1-D row partition (src/dist_spmm_node.cu:82-99)
   t0 = now_ms();
@@ -154,6 +160,7 @@ extern "C" int dsp_run(const dsp_args *A, dsp_report *rep) {
     d.needed_offsets = per_rank ? off[(size_t)p].data() : moff.data();
     d.needed_cols = per_rank ? need[(size_t)p].data() : merged.data();
     d.n_slice = &n_slice[(size_t)p * T];
+    d.pipeline = pipeline;
     if ((rc = dsp_rank_create(&d, &ranks[(size_t)p].r))) return rc;
     if (A->b_ones) {
       float *B = nullptr;

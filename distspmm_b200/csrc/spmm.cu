@@ -151,6 +151,13 @@ __host__ __device__ constexpr int entries_per_lane() {
   return 32 / LPR < 8 ? 32 / LPR : 8;
 }
 
+// Whether output row `row` adds to C: the launch accumulates, or (split pipeline) an
+// earlier phase already wrote the row.
+template <bool kAccum>
+__device__ __forceinline__ bool accumulates(const SpmmArgs &a, int32_t row) {
+  return kAccum || (a.first_phase != nullptr && (int)a.first_phase[row] < a.phase);
+}
+
 // Write one output row held in acc: to its partial slot, or to C (adding C when
 // accumulating). col0 is this lane's first column.
 template <int LPR, int VPL, int W, bool kAccum>
@@ -167,12 +174,13 @@ __device__ __forceinline__ void flush_row(const SpmmArgs &a, int32_t row, int32_
     }
   } else {
     float *dst = a.C + (int64_t)row * a.ldc;
+    const bool add = accumulates<kAccum>(a, row);
 #pragma unroll
     for (int w = 0; w < VPL; ++w) {
       const int col = col0 + w * LPR * W;
       if (col < a.N) {
         T r = acc[w];
-        if (kAccum) V::add(r, V::ld(dst + col));
+        if (add) V::add(r, V::ld(dst + col));
         V::st_stream(dst + col, r);
       }
     }
@@ -337,7 +345,8 @@ __global__ void __launch_bounds__(kSpmmThreads) spmm_nnz_kernel(const SpmmArgs a
 
 // ------------------------------------------------------------------ fixup and fills
 
-// One warp per cut row: C[row] = (kAccum ? C[row] : 0) + sum of its partial slots, in order.
+// One warp per cut row: C[row] = (accumulating ? C[row] : 0) + sum of its partial slots,
+// in order.
 template <int W, bool kAccum>
 __global__ void __launch_bounds__(kSpmmThreads) spmm_fixup_kernel(const SpmmArgs a) {
   using V = Vec<W>;
@@ -348,8 +357,9 @@ __global__ void __launch_bounds__(kSpmmThreads) spmm_fixup_kernel(const SpmmArgs
   const int32_t row = a.split_row[s];
   const int32_t p0 = a.split_ptr[s], p1 = a.split_ptr[s + 1];
   float *dst = a.C + (int64_t)row * a.ldc;
+  const bool add = accumulates<kAccum>(a, row);
   for (int col = lane * W; col < a.N; col += 32 * W) {
-    T r = kAccum ? V::ld(dst + col) : V::zero();
+    T r = add ? V::ld(dst + col) : V::zero();
     for (int32_t p = p0; p < p1; ++p) V::add(r, V::ld(a.partial + (int64_t)p * a.N + col));
     V::st(dst + col, r);
   }

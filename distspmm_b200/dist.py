@@ -52,6 +52,7 @@ def global_plan(tilings: list, task_dist: int, n_rolls: int) -> GlobalPlan:
 # ---------------------------------------------------------------------------- rank
 
 FETCH_ENGINES = {"lsu": 0, "tma": 1}  # DSP_FETCH_LSU / DSP_FETCH_TMA
+PIPELINES = {"auto": 0, "rows": 1, "split": 2}  # DSP_PIPELINE_*
 
 
 class Rank:
@@ -59,7 +60,7 @@ class Rank:
 
     def __init__(self, local: Csr, rank: int, world: int, device: int, dims: int, M: int, m_lb: int,
                  plan: GlobalPlan, n_slice: np.ndarray, sparse: np.ndarray, n_streams: int = 4,
-                 fetch_engine: str = "lsu"):
+                 fetch_engine: str = "lsu", pipeline: str = "auto"):
         self.rank, self.world, self.device, self.dims, self.M = rank, world, device, dims, M
         self.m_local = local.num_rows
         self.m_lb = m_lb
@@ -78,6 +79,7 @@ class Rank:
         d.needed_cols = merged.ctypes.data_as(P(c_i32))
         d.n_slice = self._keep[2].ctypes.data_as(P(c_i32))
         d.fetch_engine = FETCH_ENGINES[fetch_engine]
+        d.pipeline = PIPELINES[pipeline]
         h = c_vp()
         call("dsp_rank_create", ctypes.byref(d), ctypes.byref(h))
         self._h = h
@@ -185,11 +187,12 @@ def fetch_view(plan: GlobalPlan, tiling, scope: str = "node") -> GlobalPlan:
 
 def make_rank(local: Csr, rank: int, world: int, device: int, dims: int, M: int, m_lb: int, tiling,
               plan: GlobalPlan, comm_type: int, platform: str = "h100", n_streams: int = 4,
-              fetch_engine: str = "lsu", fetch_scope: str = "node") -> Rank:
+              fetch_engine: str = "lsu", fetch_scope: str = "node", pipeline: str = "auto") -> Rank:
     """Selector (CommMan_hp ctor, src/comm_man.h:341-410) + rank construction."""
     view = fetch_view(plan, tiling, fetch_scope)
     sparse = planner.comm_select(comm_type, dims, view.n_col, tiling.n_slice, platform)
-    r = Rank(local, rank, world, device, dims, M, m_lb, view, tiling.n_slice, sparse, n_streams, fetch_engine)
+    r = Rank(local, rank, world, device, dims, M, m_lb, view, tiling.n_slice, sparse, n_streams, fetch_engine,
+             pipeline)
     r.sparse = sparse
     r.n_slice = tiling.n_slice
     r.n_col = view.n_col
@@ -222,7 +225,7 @@ class LocalGroup:
 def build_local_group(g: Csr, world: int, devices, dims: int, n_rolls: int = 4, task_dist: int = 2,
                       comm_type: int = 2, platform: str = "h100", n_streams: int = 4,
                       fetch_engine: str = "lsu", partition: str = "rows",
-                      fetch_scope: str = "node") -> LocalGroup:
+                      fetch_scope: str = "node", pipeline: str = "auto") -> LocalGroup:
     """All `world` ranks of the pipeline in this process; devices[p] is rank p's GPU
     (ranks may share one). Peers read each other's B directly (same device, or peer
     access between devices)."""
@@ -233,7 +236,7 @@ def build_local_group(g: Csr, world: int, devices, dims: int, n_rolls: int = 4, 
     tilings = [planner.tile(loc, T) for loc in locals_]
     plan = global_plan(tilings, task_dist, n_rolls)
     ranks = [make_rank(locals_[p], p, world, devices[p], dims, M, bounds[p][0], tilings[p], plan, comm_type,
-                       platform, n_streams, fetch_engine, fetch_scope) for p in range(world)]
+                       platform, n_streams, fetch_engine, fetch_scope, pipeline) for p in range(world)]
     for p in range(world):
         for q in range(world):
             if p != q:

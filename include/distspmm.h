@@ -280,7 +280,22 @@ typedef struct dsp_rank_desc {
   const int32_t *needed_cols;    /* tile-local ids, ascending per tile          */
   const int32_t *n_slice;        /* [T] n_slice_list of this rank               */
   int fetch_engine;              /* DSP_FETCH_LSU (default) or DSP_FETCH_TMA     */
+  int pipeline;                  /* DSP_PIPELINE_* (0 = pick from the matrix)    */
 } dsp_rank_desc;
+
+/* How a rank's nonzeros are cut into phases, phase k running once the fetches of ring
+ * positions 1..k (peer (rank + k) % P) have landed:
+ *   ROWS   whole rows, in the phase of the last ring position their columns need: every C
+ *          row written once (no read-modify-write); best when most rows need only owned
+ *          tiles (banded / mesh matrices).
+ *   SPLIT  nonzeros by the ring position owning their column, as the reference's per-tile
+ *          loop (src/dist_spmm_node.cu:329-394): a row is written in its first phase and
+ *          accumulated in later ones, so compute overlaps every fetch; best when nearly all
+ *          rows need remote tiles (power-law graphs).
+ *   AUTO   SPLIT when less than half the nonzeros fall in ROWS's phase 0. */
+#define DSP_PIPELINE_AUTO 0
+#define DSP_PIPELINE_ROWS 1
+#define DSP_PIPELINE_SPLIT 2
 
 /* Sparse-fetch engines: LSU = warps with 128-bit peer loads, one block per SM next to the
  * SpMM; TMA = per-row cp.async.bulk copies through a shared-memory ring (no multicast). */
@@ -299,6 +314,8 @@ typedef struct dsp_rank_stats {
   int64_t launches_per_step; /* kernels + copies enqueued per step               */
   int64_t kernels_per_step;  /* of which kernels of this library                  */
   int64_t device_bytes;      /* device memory held by the rank                   */
+  int64_t pipeline;          /* DSP_PIPELINE_ROWS or DSP_PIPELINE_SPLIT in use   */
+  int64_t phase0_nnz;        /* nonzeros computed before any fetch lands         */
 } dsp_rank_stats;
 
 int dsp_rank_create(const dsp_rank_desc *d, dsp_rank **out);

@@ -25,11 +25,11 @@ def _devices(world):
 
 
 def _run_group(A, world, dims, rolls, task_dist, comm_type, seed=21, poison=True, fetch_engine="lsu",
-               partition="rows", fetch_scope="node"):
+               partition="rows", fetch_scope="node", pipeline="auto"):
     import torch
     from distspmm_b200.dist import build_local_group
     g = build_local_group(A, world, _devices(world), dims, rolls, task_dist, comm_type, fetch_engine=fetch_engine,
-                          partition=partition, fetch_scope=fetch_scope)
+                          partition=partition, fetch_scope=fetch_scope, pipeline=pipeline)
     for r in g.ranks:
         if poison:
             r.poison_remote()
@@ -150,6 +150,61 @@ def test_group_parity_partition_and_fetch_scope(gpu, rmat12, partition, fetch_sc
             remote = sum(int(t.n_col[k]) for k in range(g.plan.T)
                          if g.plan.remap[k] != r.rank and t.nnz[k] > 0)
             assert r.stats()["fetch_rows"] == remote
+    g.close()
+
+
+@pytest.mark.parametrize("pipeline", ["rows", "split"])
+@pytest.mark.parametrize("world,comm_type,partition", [(2, 2, "rows"), (3, 1, "balanced"), (4, 0, "balanced"),
+                                                       (8, 2, "balanced")])
+def test_group_parity_pipelines(gpu, rmat12, pipeline, world, comm_type, partition):
+    """Both phase structures give the oracle's C: whole rows after their last fetch, or
+    nonzeros per ring position with rows written by their first phase and accumulated by
+    later ones (remote rows NaN-poisoned before the step)."""
+    g, C = _run_group(rmat12, world, 128, 4, 2, comm_type, partition=partition, fetch_scope="rank",
+                      pipeline=pipeline)
+    _check(rmat12, C, 128)
+    assert all(r.stats()["pipeline"] == (1 if pipeline == "rows" else 2) for r in g.ranks)
+    g.close()
+
+
+@pytest.mark.parametrize("dims", [4, 100, 256])
+def test_group_split_pipeline_widths(gpu, rmat12, dims):
+    g, C = _run_group(rmat12, 4, dims, 2, 2, 2, pipeline="split")
+    _check(rmat12, C, dims)
+    g.close()
+
+
+def _auto_pipeline(g, p, A):
+    """The AUTO rule restated: split when whole rows would leave most nonzeros behind the
+    fetches (rows-pipeline phase 0 < 1/2) and the owned tiles hold >= 30 % of them."""
+    lb, ub = g.bounds[p]
+    ip = np.asarray(A.indptr[lb:ub + 1]) - A.indptr[lb]
+    cols = np.asarray(A.indices[A.indptr[lb]:A.indptr[ub]])
+    pos = (g.plan.remap[cols // g.plan.cpt] - p) % len(g.ranks)
+    rowid = np.repeat(np.arange(ub - lb), np.diff(ip))
+    last = np.full(ub - lb, -1)
+    np.maximum.at(last, rowid, pos)
+    phase0 = int(np.diff(ip)[last == 0].sum())
+    local = int((pos == 0).sum())
+    nnz = int(ip[-1])
+    return 2 if (2 * phase0 < nnz and 10 * local >= 3 * nnz) else 1
+
+
+def test_pipeline_auto_choice(gpu, rmat12):
+    """AUTO follows its rule on R-MAT; a stencil stays on whole rows (most rows need only
+    owned tiles); a uniform matrix on 2 ranks splits (half of every row local, every row
+    needing the peer)."""
+    from distspmm_b200.dist import build_local_group
+    g = build_local_group(rmat12, 4, _devices(4), 64, 4, 2, 2, partition="balanced", fetch_scope="rank")
+    assert [r.stats()["pipeline"] for r in g.ranks] == [_auto_pipeline(g, p, rmat12) for p in range(4)]
+    g.close()
+    U = d.gen_uniform(4096, 32, seed=3)
+    g = build_local_group(U, 2, _devices(2), 64, 4, 2, 2, partition="balanced", fetch_scope="rank")
+    assert [r.stats()["pipeline"] for r in g.ranks] == [2] * 2
+    g.close()
+    A = d.gen_stencil27(20, seed=4)
+    g = build_local_group(A, 4, _devices(4), 64, 4, 2, 2, partition="balanced", fetch_scope="rank")
+    assert [r.stats()["pipeline"] for r in g.ranks] == [1] * 4
     g.close()
 
 
