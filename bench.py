@@ -66,6 +66,8 @@ def parse_args(argv=None):
     ap.add_argument("--pipeline", choices=["auto", "rows", "split"], default="auto",
                     help="phases: whole rows after their last fetch, nonzeros per ring position, or per matrix")
     ap.add_argument("--fetch-streams", type=int, default=4, help="concurrent fetch streams (nvlink_num_producers)")
+    ap.add_argument("--platform", choices=["h100", "a800", "b200"], default="b200",
+                    help="adaptive selector constants (comm_type 2); b200 = the NVLink 5 fit of comm_test")
     ap.add_argument("--seed", type=int, default=1)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -110,7 +112,7 @@ def config_of(a, world, nnz, M):
             "rows": M, "nnz": nnz, "dims": a.dims, "n_rolls": a.n_rolls, "task_dist": a.task_dist,
             "comm_type": a.comm_type, "parallelism": f"row1d_p{world}", "seed": a.seed,
             "partition": a.partition if world > 1 else "single rank", "fetch_scope": a.fetch_scope,
-            "pipeline": a.pipeline, "fetch_streams": a.fetch_streams,
+            "pipeline": a.pipeline, "fetch_streams": a.fetch_streams, "selector_platform": a.platform,
             "l2": "flushed between steps (512 MiB write)" if not a.no_flush else "not flushed",
             "b": "U(-1,1) fp32 row-major"}
 
@@ -309,7 +311,7 @@ def main(argv=None):
         plan = global_plan([tiling], a.task_dist, a.n_rolls)
     else:
         tiling, plan = distributed_plan(comm, local, a.n_rolls, a.task_dist)
-    R = make_rank(local, rank, world, local_rank, a.dims, M, lb, tiling, plan, a.comm_type, "h100", a.fetch_streams,
+    R = make_rank(local, rank, world, local_rank, a.dims, M, lb, tiling, plan, a.comm_type, a.platform, a.fetch_streams,
                   fetch_scope=a.fetch_scope, pipeline=a.pipeline)
     if comm is not None:
         connect_peers(comm, R)

@@ -131,6 +131,8 @@ PROTOTYPES = {
     "dsp_rank_step": (c_int, [c_vp, c_vp]),
     "dsp_rank_check_error": (c_int, [c_vp]),
     "dsp_selftest_bounded_wait": (c_int, [ctypes.c_longlong, P(c_int)]),
+    "dsp_comm_probe": (c_int, [c_int, c_int, c_i64, c_int, P(c_i32), c_int, P(c_i64), c_int, c_int, P(c_f64),
+                               P(c_f64)]),
     "dsp_rank_download_c": (c_int, [c_vp, c_vp, c_vp]),
     "dsp_rank_last_compute_ms": (c_int, [c_vp, P(c_f32)]),
     "dsp_rank_last_timeline": (c_int, [c_vp, P(c_f32), c_int]),

@@ -266,3 +266,98 @@ extern "C" int dsp_selftest_bounded_wait(long long budget_cycles, int *code_out)
   *code_out = v;
   return v != 0 ? dsp::fail(DSP_ERR_TIMEOUT, "bounded wait gave up as designed (code %d)", v) : DSP_OK;
 }
+
+// ------------------------------------------------------------------ bulk vs sparse fetch probe
+//
+// The reference's comm_test microbenchmark (src/comm_test.cu:83-147) on this engine's two
+// fetch paths: one copy-engine copy of a peer's whole rows x dims buffer (the bulk tile
+// fetch) against the sparse fetch of the first counts[i] rows of `row_ids` (the gather
+// kernel of `engine`), both from peer_device's memory into device's, timed with CUDA events
+// on one stream (mean of `reps` launches after one untimed launch).
+extern "C" int dsp_comm_probe(int device, int peer_device, int64_t rows, int dims, const int32_t *row_ids,
+                              int n_counts, const int64_t *counts, int engine, int reps, double *bulk_ms,
+                              double *sparse_ms) {
+  using namespace dsp;
+  DSP_TRY_ARG(rows >= 1 && rows <= INT32_MAX && dims >= 1 && row_ids && n_counts >= 0 && (n_counts == 0 || counts) &&
+                  reps >= 1 && bulk_ms && (n_counts == 0 || sparse_ms),
+              "dsp_comm_probe: bad argument");
+  int64_t max_n = 0;
+  for (int i = 0; i < n_counts; ++i) {
+    DSP_TRY_ARG(counts[i] >= 0 && counts[i] <= rows, "dsp_comm_probe: counts[%d] = %lld", i, (long long)counts[i]);
+    max_n = std::max(max_n, counts[i]);
+  }
+  for (int64_t i = 0; i < max_n; ++i)
+    DSP_TRY_ARG(row_ids[i] >= 0 && row_ids[i] < rows, "dsp_comm_probe: row_ids[%lld] = %d", (long long)i, row_ids[i]);
+  int prev = 0;
+  cudaGetDevice(&prev);
+  const size_t bytes = sizeof(float) * (size_t)rows * (size_t)dims;
+  float *src = nullptr, *dst = nullptr;
+  int32_t *d_rows = nullptr;
+  int *d_err = nullptr;
+  cudaStream_t s = nullptr;
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  int rc = DSP_OK;
+  cudaError_t e = cudaSetDevice(peer_device);
+  if (e == cudaSuccess) e = cudaMalloc(&src, bytes);
+  if (e == cudaSuccess) e = cudaMemset(src, 0, bytes);
+  if (e == cudaSuccess) e = cudaSetDevice(device);
+  if (e == cudaSuccess && peer_device != device) {
+    e = cudaDeviceEnablePeerAccess(peer_device, 0);
+    if (e == cudaErrorPeerAccessAlreadyEnabled) {
+      cudaGetLastError();
+      e = cudaSuccess;
+    }
+  }
+  if (e == cudaSuccess) e = cudaMalloc(&dst, bytes);
+  if (e == cudaSuccess) e = cudaMalloc(&d_rows, sizeof(int32_t) * (size_t)std::max<int64_t>(max_n, 1));
+  if (e == cudaSuccess && max_n > 0)
+    e = cudaMemcpy(d_rows, row_ids, sizeof(int32_t) * (size_t)max_n, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMalloc(&d_err, sizeof(int));
+  if (e == cudaSuccess) e = cudaMemset(d_err, 0, sizeof(int));
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaEventCreate(&e0);
+  if (e == cudaSuccess) e = cudaEventCreate(&e1);
+  if (e != cudaSuccess) rc = fail(DSP_ERR_CUDA, "dsp_comm_probe set-up: %s", cudaGetErrorString(e));
+
+  auto timed = [&](auto &&launch, double *out) -> int {
+    int r = launch();
+    if (r) return r;
+    cudaEventRecord(e0, s);
+    for (int k = 0; k < reps && r == DSP_OK; ++k) r = launch();
+    cudaEventRecord(e1, s);
+    cudaError_t ee = cudaEventSynchronize(e1);
+    if (r) return r;
+    if (ee != cudaSuccess) return fail(DSP_ERR_CUDA, "dsp_comm_probe: %s", cudaGetErrorString(ee));
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, e0, e1);
+    *out = (double)ms / reps;
+    return DSP_OK;
+  };
+  if (rc == DSP_OK)
+    rc = timed(
+        [&]() -> int {
+          cudaError_t ce = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, s);
+          return ce == cudaSuccess ? DSP_OK : fail(DSP_ERR_CUDA, "bulk copy: %s", cudaGetErrorString(ce));
+        },
+        bulk_ms);
+  for (int i = 0; i < n_counts && rc == DSP_OK; ++i)
+    rc = timed([&]() { return launch_gather_rows(dst, src, d_rows, counts[i], dims, engine, d_err, s); }, &sparse_ms[i]);
+  if (rc == DSP_OK) {
+    int flag = 0;
+    cudaMemcpy(&flag, d_err, sizeof flag, cudaMemcpyDeviceToHost);
+    if (flag) rc = fail(DSP_ERR_TIMEOUT, "dsp_comm_probe: a fetch wait gave up (code %d)", flag);
+  }
+  if (s) cudaStreamSynchronize(s);
+  if (e0) cudaEventDestroy(e0);
+  if (e1) cudaEventDestroy(e1);
+  if (s) cudaStreamDestroy(s);
+  if (d_err) cudaFree(d_err);
+  if (d_rows) cudaFree(d_rows);
+  if (dst) cudaFree(dst);
+  if (src) {
+    cudaSetDevice(peer_device);
+    cudaFree(src);
+  }
+  cudaSetDevice(prev);
+  return rc;
+}

@@ -283,9 +283,11 @@ extern "C" int dsp_comm_model_preset(int platform, int tier, dsp_comm_model *out
     const double inter[4] = {1440.80, -1394.99, 43.65, -1.00};
     memcpy(p, tier == DSP_TIER_INTRA ? intra : inter, sizeof p);
   } else if (platform == DSP_PLATFORM_B200) {
-    // Until a B200 NVLink 5 fit exists the B200 preset keeps the H100 constants; the
-    // inter-node tier does not exist on one 8-GPU box.
-    const double intra[4] = {12873.61472, 125.27085, 105.50392, -4.65};
+    // Intra: fit (distspmm_b200.fit_comm_model) of the critical densities measured by
+    // distspmm_b200.comm_test between two B200s over NVLink 5 (N = 400k, 1000k, 1400k,
+    // 1800k; dims 1..1024): the sparse gather wins up to ~0.9 density from 128 columns on.
+    // Inter: the InfiniBand tier cannot be measured on one 8-GPU box; H100's constants.
+    const double intra[4] = {0.03045, 100.87679, 130.98926, 0.49};
     const double inter[4] = {1452.17110, -1407.82558, 47.34021, -1.00};
     memcpy(p, tier == DSP_TIER_INTRA ? intra : inter, sizeof p);
   } else {

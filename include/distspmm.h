@@ -173,7 +173,9 @@ typedef struct dsp_comm_model {
 
 #define DSP_PLATFORM_H100 0 /* default of the reference (src/comm_man.h:391-394) */
 #define DSP_PLATFORM_A800 1 /* DISTSPMM_PLATFORM_A800 (src/comm_man.h:387-390)    */
-#define DSP_PLATFORM_B200 2 /* refit on B200 NVLink 5; see DESIGN notes           */
+#define DSP_PLATFORM_B200 2 /* intra: fit of dsp_comm_probe on B200 NVLink 5     */
+                            /* (a, b, c, u = 0.03045, 100.87679, 130.98926, 0.49); */
+                            /* inter: H100's (no second node to measure)          */
 #define DSP_TIER_INTRA 0
 #define DSP_TIER_INTER 1
 int dsp_comm_model_preset(int platform, int tier, dsp_comm_model *out);
@@ -351,6 +353,15 @@ int dsp_rank_check_error(dsp_rank *r);
  * records code 3 and returns. Returns DSP_ERR_TIMEOUT with *code_out = 3 when the wait gave
  * up as designed, DSP_OK if it (impossibly) completed. No fault, no hang. */
 int dsp_selftest_bounded_wait(long long budget_cycles, int *code_out);
+/* Bulk-vs-sparse fetch microbenchmark, the reference's comm_test (src/comm_test.cu:83-147)
+ * on this engine's fetch paths: *bulk_ms = one copy-engine copy of peer_device's whole
+ * rows x dims fp32 buffer into device; sparse_ms[i] = the gather kernel of `engine`
+ * (DSP_FETCH_*) moving the first counts[i] rows of row_ids (host, < rows) the same way.
+ * Mean of `reps` timed launches (CUDA events) after one untimed launch; the buffers are
+ * allocated and freed by the call. peer_device == device measures a local copy. */
+int dsp_comm_probe(int device, int peer_device, int64_t rows, int dims, const int32_t *row_ids,
+                   int n_counts, const int64_t *counts, int engine, int reps, double *bulk_ms,
+                   double *sparse_ms);
 /* Copy C (m_local x dims) to host. */
 int dsp_rank_download_c(dsp_rank *r, float *C_host, void *stream);
 /* Device time (ms) of the SpMM kernels of the last step, from CUDA events on the compute

@@ -14,6 +14,9 @@ Fixtures and their source of truth:
                        src/comm_man.h:396-400 evaluated by an nvcc-compiled probe
                        (oracle/threshold_probe.cu), bit patterns, for the H100 and A800
                        constants and dims 1..2048.
+  comm_model_fit.json  the reference's own model fit (tools/fit_comm_model.py, imported
+                       from the reference tree): the (dims, mean critical density) inputs
+                       it fits per tier and the (a, b, c, u) it returns.
 Nothing here runs on the GPU box; the tests only read the committed files.
 """
 from __future__ import annotations
@@ -88,7 +91,23 @@ def make_thresholds():
         json.dump(res, f, indent=1)
 
 
+def make_fit(ref_root="/root/reference"):
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("ref_fit", os.path.join(ref_root, "tools", "fit_comm_model.py"))
+    ref = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(ref)
+    params = ref.fit_all()
+    group0 = [0, 2, 4, 6]  # the runs the reference averages before fitting (fit_all)
+    out = {"dims": list(ref.DIMS)}
+    for tier, col in (("intra", 1), ("inter", 2)):
+        out[tier] = {"threshold": np.mean([ref.MEASURED[i][col] for i in group0], axis=0).tolist(),
+                     "params": [float(x) for x in params[tier]]}
+    with open(os.path.join(HERE, "comm_model_fit.json"), "w") as f:
+        json.dump(out, f, indent=1)
+
+
 if __name__ == "__main__":
+    make_fit()
     oracle.build(ref=True)
     if oracle.ref_lib() is None:
         sys.exit("reference shim not available: run where the reference sources exist")
