@@ -99,6 +99,9 @@ PROTOTYPES = {
     "dsp_partition": (c_int, [P(dsp_csr), c_i64, c_i64, P(dsp_csr)]),
     "dsp_tile_counts": (c_int, [P(dsp_csr), c_int, P(c_i64), P(c_i32), P(c_i32), P(c_i64)]),
     "dsp_tile_needed": (c_int, [P(dsp_csr), c_int, P(c_i64), P(c_i32)]),
+    "dsp_col_presence": (c_int, [c_vp, c_i64, c_i64, c_vp, c_vp]),
+    "dsp_tile_device": (c_int, [c_vp, c_i64, c_vp, c_i64, c_int, P(c_i64), P(c_i32), P(c_i32), P(c_i64), P(c_i64),
+                                P(c_i32), c_vp]),
     "dsp_hsdma": (c_int, [P(c_i32), c_int, c_int, P(c_i32), c_int, c_int, c_int, P(c_i32)]),
     "dsp_alloc_slice": (c_int, [c_int, c_int, P(c_i32)]),
     "dsp_alloc_random": (c_int, [c_int, c_int, c_u64, P(c_i32)]),

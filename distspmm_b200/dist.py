@@ -298,12 +298,18 @@ class TorchComm:
             self.dist.barrier(group=self.group)
 
 
-def distributed_plan(comm, local: Csr, n_rolls: int, task_dist: int):
+def distributed_plan(comm, local: Csr, n_rolls: int, task_dist: int, device_setup: bool = False):
     """This rank's tiling plus the agreed global plan, via host collectives: every rank
     contributes its demand row and needed lists; the allocation is computed from the
     gathered demand (identically on every rank, which equals the reference's root
-    compute + broadcast)."""
+    compute + broadcast).
+
+    device_setup (NCCL groups): tile on the GPU from a column-presence byte map and form
+    the node union as an all-reduce MAX of the ranks' maps instead of all-gathering the
+    lists; same plan."""
     T = comm.world * n_rolls
+    if device_setup:
+        return _distributed_plan_device(comm, local, n_rolls, task_dist)
     mine = planner.tile(local, T)
     n_cols = comm.allgather_i32(mine.n_col)
     needed = comm.allgather_i32(mine.needed)
@@ -315,6 +321,27 @@ def distributed_plan(comm, local: Csr, n_rolls: int, task_dist: int):
     tilings = [_T(n_cols[p], needed[p], mine.cpt) for p in range(comm.world)]
     plan = global_plan(tilings, task_dist, n_rolls)
     return mine, plan
+
+
+def _distributed_plan_device(comm, local: Csr, n_rolls: int, task_dist: int):
+    import time
+
+    torch = comm.torch
+    if comm.device.type != "cuda":
+        raise RuntimeError("device_setup needs an NCCL process group (CUDA tensors)")
+    T = comm.world * n_rolls
+    M = local.num_cols
+    d_cols = torch.from_numpy(np.ascontiguousarray(local.indices, np.int64)).to(comm.device)
+    stream = torch.cuda.current_stream(comm.device).cuda_stream
+    present = planner.col_presence(d_cols, M, stream)
+    mine = planner.tile_device(d_cols, M, T, present, stream)
+    demand = np.stack(comm.allgather_i32(mine.n_col)).astype(np.int32)
+    comm.dist.all_reduce(present, op=comm.dist.ReduceOp.MAX, group=comm.group)  # node union
+    n, off, merged = planner.needed_from_presence(present, M, T, stream)
+    t0 = time.perf_counter()
+    remap = planner.allocate(task_dist, demand, n_rolls)
+    hs = (time.perf_counter() - t0) * 1e3 if task_dist == 2 else 0.0
+    return mine, GlobalPlan(T, mine.cpt, remap, n, off, merged, hs, demand)
 
 
 def connect_peers(comm, rank: Rank) -> None:

@@ -92,6 +92,44 @@ def tile(local: Csr, T: int) -> Tiling:
     return Tiling(int(cpt.value), n_col, n_slice, nnz, off, needed[: int(off[-1])])
 
 
+def col_presence(d_cols, num_cols: int, stream: int = 0):
+    """Device byte map of the columns in d_cols (a CUDA int64 tensor): 1 where present."""
+    import torch
+    present = torch.empty(num_cols, dtype=torch.uint8, device=d_cols.device)
+    call("dsp_col_presence", d_cols.data_ptr(), d_cols.numel(), num_cols, present.data_ptr(), stream)
+    return present
+
+
+def tile_device(d_cols, num_cols: int, T: int, present=None, stream: int = 0) -> Tiling:
+    """tile() computed on the GPU from the local column ids already in device memory (a
+    CUDA int64 tensor); `present` (their col_presence map) is reused when given."""
+    cpt = c_i64()
+    n_col = np.zeros(T, np.int32)
+    n_slice = np.zeros(T, np.int32)
+    nnz = np.zeros(T, np.int64)
+    off = np.zeros(T + 1, np.int64)
+    pp = present.data_ptr() if present is not None else None
+    call("dsp_tile_device", d_cols.data_ptr(), d_cols.numel(), pp, num_cols, T, ctypes.byref(cpt), _ptr(n_col, c_i32),
+         _ptr(n_slice, c_i32), _ptr(nnz, c_i64), _ptr(off, c_i64), None, stream)
+    needed = np.zeros(max(int(off[-1]), 1), np.int32)
+    call("dsp_tile_device", d_cols.data_ptr(), d_cols.numel(), pp, num_cols, T, None, None, None, None,
+         _ptr(off, c_i64), _ptr(needed, c_i32), stream)
+    return Tiling(int(cpt.value), n_col, n_slice, nnz, off, needed[: int(off[-1])])
+
+
+def needed_from_presence(present, num_cols: int, T: int, stream: int = 0):
+    """(n_col, offsets, ascending tile-local lists) of a device presence map; with the
+    element-wise max of the ranks' maps this is the node union of merge_needed."""
+    n_col = np.zeros(T, np.int32)
+    off = np.zeros(T + 1, np.int64)
+    call("dsp_tile_device", None, 0, present.data_ptr(), num_cols, T, None, _ptr(n_col, c_i32), None, None,
+         _ptr(off, c_i64), None, stream)
+    cols = np.zeros(max(int(off[-1]), 1), np.int32)
+    call("dsp_tile_device", None, 0, present.data_ptr(), num_cols, T, None, None, None, None, _ptr(off, c_i64),
+         _ptr(cols, c_i32), stream)
+    return n_col, off, cols[: int(off[-1])]
+
+
 def hierarchical_iterative_refinement_allocation(demand, node_of_gpu, tasks_per_gpu: int,
                                                  max_inter_node_iterations: int = 5,
                                                  max_intra_node_iterations: int = 5) -> np.ndarray:

@@ -141,6 +141,23 @@ int dsp_tile_counts(const dsp_csr *local, int T, int64_t *cpt_out, int32_t *n_co
  * entries and is written by this call; cols must hold sum(n_col_list) ints. */
 int dsp_tile_needed(const dsp_csr *local, int T, int64_t *offsets, int32_t *cols);
 
+/* The same tiling on the current GPU, replacing the reference's per-nonzero unordered_set
+ * loop (src/dist_spmm_node.cu:103-132). dsp_col_presence: d_present[c] = 1 for every column
+ * c of the nnz device column ids d_cols (int64, the reference's index type), 0 elsewhere
+ * (num_cols bytes, device); DSP_ERR_FORMAT if an id lies outside [0, num_cols).
+ * Synchronous on `stream`. */
+int dsp_col_presence(const int64_t *d_cols, int64_t nnz, int64_t num_cols, uint8_t *d_present,
+                     void *stream);
+/* Counts and ascending needed lists of dsp_tile_counts / dsp_tile_needed from device data:
+ * n_col_list and the lists from d_present (computed from d_cols when NULL), n_slice_list and
+ * nnz_list from d_cols (may be NULL when those outputs are). Node merge: pass the
+ * element-wise maximum of the ranks' presence maps (an all-reduce, e.g. NCCL MAX on
+ * uint8) as d_present and get the union lists of dsp_merge_needed. Outputs are host arrays
+ * (any may be NULL; cols needs offsets and holds offsets[T] ids). T <= 8192. Synchronous. */
+int dsp_tile_device(const int64_t *d_cols, int64_t nnz, const uint8_t *d_present, int64_t num_cols,
+                    int T, int64_t *cpt_out, int32_t *n_col_list, int32_t *n_slice_list,
+                    int64_t *nnz_list, int64_t *offsets, int32_t *cols, void *stream);
+
 /* HSDMA two-phase greedy swap refinement (hierarchical_iterative_refinement_allocation,
  * src/h_sdma.h:78-228). demand is the P x T row-major matrix of pre-merge n_col_list
  * rows (rank-major), node_of_gpu[P] the node id of each rank (ranks of a node

@@ -20,7 +20,7 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, out_dir, comm_type, dims):
+def _worker(rank, world, port, out_dir, comm_type, dims, device_setup=False):
     import datetime
 
     import torch
@@ -38,6 +38,13 @@ def _worker(rank, world, port, out_dir, comm_type, dims):
     lb, ub = planner.partition_bounds(A.num_rows, world, rank)
     local = planner.partition(A, lb, ub)
     tiling, plan = distributed_plan(comm, local, 4, 2)
+    if device_setup:  # the GPU set-up path must agree with the host planner exactly
+        t2, p2 = distributed_plan(comm, local, 4, 2, device_setup=True)
+        for f in ("n_col", "n_slice", "nnz", "offsets", "needed"):
+            assert np.array_equal(getattr(t2, f), getattr(tiling, f)), f
+        for f in ("remap", "n_col", "offsets", "merged", "demand"):
+            assert np.array_equal(getattr(p2, f), getattr(plan, f)), f
+        tiling, plan = t2, p2
     R = make_rank(local, rank, world, rank, dims, A.num_rows, lb, tiling, plan, comm_type)
     connect_peers(comm, R)
     for it in range(2):
@@ -60,8 +67,9 @@ def _worker(rank, world, port, out_dir, comm_type, dims):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("comm_type,dims", [(2, 128), (0, 64), (1, 32)])
-def test_two_process_pipeline(gpu, comm_type, dims):
+@pytest.mark.parametrize("comm_type,dims,device_setup", [(2, 128, False), (0, 64, False), (1, 32, False),
+                                                        (2, 128, True)])
+def test_two_process_pipeline(gpu, comm_type, dims, device_setup):
     import torch
     import torch.multiprocessing as mp
 
@@ -72,7 +80,7 @@ def test_two_process_pipeline(gpu, comm_type, dims):
         pytest.skip("needs 2 or more GPUs")
     world = min(world, 4)
     with tempfile.TemporaryDirectory() as tmp:
-        mp.start_processes(_worker, args=(world, _free_port(), tmp, comm_type, dims), nprocs=world,
+        mp.start_processes(_worker, args=(world, _free_port(), tmp, comm_type, dims, device_setup), nprocs=world,
                            start_method="spawn", join=True)
         A = d.gen_rmat(14, seed=5)
         C = np.concatenate([np.load(os.path.join(tmp, f"c{r}.npy")) for r in range(world)])
