@@ -155,9 +155,7 @@ extern "C" int dsp_tile_device(const int64_t *d_cols, int64_t nnz, const uint8_t
                                int64_t *offsets, int32_t *cols, void *stream) {
   DSP_TRY_ARG(num_cols >= 1 && T >= 1 && nnz >= 0, "dsp_tile_device: bad argument");
   DSP_TRY_ARG(T <= kMaxTilesDevice, "dsp_tile_device: T = %d exceeds %d", T, kMaxTilesDevice);
-  DSP_TRY_ARG(d_cols || (nnz == 0 && !n_slice_list && !nnz_list),
-              "dsp_tile_device: n_slice / nnz lists need the column ids");
-  DSP_TRY_ARG(d_present || d_cols || nnz == 0, "dsp_tile_device: no presence map and no column ids");
+  DSP_TRY_ARG(d_cols || nnz == 0, "dsp_tile_device: %lld nonzeros without column ids", (long long)nnz);
   DSP_TRY_ARG(!cols || offsets, "dsp_tile_device: cols needs offsets");
   cudaStream_t s = (cudaStream_t)stream;
   const int64_t cpt = (num_cols + T - 1) / T;  // src/dist_spmm_node.cu:106

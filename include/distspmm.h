@@ -150,7 +150,7 @@ int dsp_col_presence(const int64_t *d_cols, int64_t nnz, int64_t num_cols, uint8
                      void *stream);
 /* Counts and ascending needed lists of dsp_tile_counts / dsp_tile_needed from device data:
  * n_col_list and the lists from d_present (computed from d_cols when NULL), n_slice_list and
- * nnz_list from d_cols (may be NULL when those outputs are). Node merge: pass the
+ * nnz_list from d_cols (NULL with nnz = 0: no nonzeros, all zero). Node merge: pass the
  * element-wise maximum of the ranks' presence maps (an all-reduce, e.g. NCCL MAX on
  * uint8) as d_present and get the union lists of dsp_merge_needed. Outputs are host arrays
  * (any may be NULL; cols needs offsets and holds offsets[T] ids). T <= 8192. Synchronous. */
