@@ -462,8 +462,15 @@ def main(argv=None):
               "achieved": round(gathered / (mean_compute * 1e-3) / 1e9, 1)}
 
     fetch_bytes = st["fetch_bytes"]
+    # per rank: nonzeros, rows, phase structure, SpMM time, time waiting for fetches, bytes
+    mine = [st["nnz_local"], st["m_local"], st["pipeline"], int(mean_compute * 1e4), int(idle * 1e4),
+            st["fetch_bytes"] // 1024]
+    per_rank = [mine]
     if comm is not None:
         fetch_bytes = comm.allreduce_sum_i64(fetch_bytes)
+        per_rank = [[int(x) for x in r] for r in comm.allgather_i32(np.array(mine, np.int64).clip(max=2**31 - 1))]
+    ranks = [{"nnz": r[0], "rows": r[1], "pipeline": ["", "rows", "split"][r[2]], "compute_ms": r[3] / 1e4,
+              "idle_ms": r[4] / 1e4, "fetched_kib": r[5]} for r in per_rank]
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": a.steps,
         "warmup": a.warmup, "ms_per_step": round(t_step, 4), "higher_is_better": True, "scaling": "strong",
@@ -479,7 +486,7 @@ def main(argv=None):
                    "phase0_nnz_rank0": st["phase0_nnz"],
                    "max_rank_compute_ms": round(t_comp_max, 4),
                    "max_rank_compute_idle_ms": round(idle_max, 4),
-                   "timeline_rank0": timeline if rank == 0 else None},
+                   "timeline_rank0": timeline if rank == 0 else None, "ranks": ranks},
         "wall_s_timed_region": round(wall, 3),
         "gather": gather,
     }

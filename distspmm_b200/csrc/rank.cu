@@ -156,16 +156,20 @@ int build_phases(dsp_rank *r, const dsp_csr *a, int pipeline) {
   const int P = r->P, me = r->me;
   const int64_t m = a->num_rows, cpt = r->cpt;
   std::vector<int32_t> phase((size_t)std::max<int64_t>(m, 1), -1), first((size_t)std::max<int64_t>(m, 1), -1);
+  std::vector<uint8_t> touched((size_t)std::max<int64_t>(m, 1), 0);  // ring positions per row (P <= 64)
   parallel_for(m, [&](int64_t b, int64_t e) {
     for (int64_t i = b; i < e; ++i) {
       int32_t ph = -1, lo = P;
+      uint64_t seen = 0;
       for (int64_t j = a->indptr[i]; j < a->indptr[i + 1]; ++j) {
         const int32_t k = (r->remap[(size_t)(a->indices[j] / cpt)] - me + P) % P;
         ph = std::max(ph, k);
         lo = std::min(lo, k);
+        if (k < 64) seen |= 1ull << k;
       }
       phase[(size_t)i] = ph;
       first[(size_t)i] = ph < 0 ? -1 : lo;
+      touched[(size_t)i] = (uint8_t)__builtin_popcountll(seen);
     }
   }, 1024);
   std::vector<int32_t> empty;
@@ -181,14 +185,20 @@ int build_phases(dsp_rank *r, const dsp_csr *a, int pipeline) {
   }
   r->segs.resize((size_t)P);
   // nonzeros in tiles this rank owns: what the split pipeline computes before any fetch
-  int64_t local_nnz = 0;
+  int64_t local_nnz = 0, pairs = 0;
   for (int64_t j = 0; j < a->nnz; ++j) local_nnz += r->remap[(size_t)(a->indices[j] / cpt)] == me;
-  // AUTO: split only when whole rows would leave most of the work behind the fetches and
-  // the owned tiles hold enough work (>= 30 %) to hide them; measured on B200 at P = 2:
-  // R-MAT (16 % local, hub rows) runs 20 % slower split, the stencil is rows-bound.
+  for (int64_t i = 0; i < m; ++i) pairs += touched[(size_t)i];  // (row, phase) pieces in split
+  // AUTO: split only when whole rows would leave most of the work behind the fetches, the
+  // owned tiles hold enough work (>= 30 %) to hide them, and a row's piece per phase is long
+  // (>= 12 nonzeros): every extra piece costs a read-modify-write of its C row. Measured on
+  // B200: uniform 32/row at P = 2 (50 % local, 16 per piece) +10 % split; R-MAT at P = 2
+  // (16 % local) and P = 4 (short pieces on the low-degree ranks) slower split; the
+  // stencil is rows-bound.
   if (pipeline == DSP_PIPELINE_AUTO)
-    pipeline = 2 * rows_phase0_nnz < a->nnz && 10 * local_nnz >= 3 * a->nnz ? DSP_PIPELINE_SPLIT : DSP_PIPELINE_ROWS;
-  if (P == 1 || P > 255) pipeline = DSP_PIPELINE_ROWS;
+    pipeline = 2 * rows_phase0_nnz < a->nnz && 10 * local_nnz >= 3 * a->nnz && a->nnz >= 12 * pairs
+                   ? DSP_PIPELINE_SPLIT
+                   : DSP_PIPELINE_ROWS;
+  if (P == 1 || P > 64) pipeline = DSP_PIPELINE_ROWS;
   r->pipeline = pipeline;
   if (pipeline == DSP_PIPELINE_SPLIT) {
     r->stats.phase0_nnz = local_nnz;
