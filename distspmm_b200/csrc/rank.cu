@@ -185,17 +185,26 @@ int build_phases(dsp_rank *r, const dsp_csr *a, int pipeline) {
   }
   r->segs.resize((size_t)P);
   // nonzeros in tiles this rank owns: what the split pipeline computes before any fetch
-  int64_t local_nnz = 0, pairs = 0;
-  for (int64_t j = 0; j < a->nnz; ++j) local_nnz += r->remap[(size_t)(a->indices[j] / cpt)] == me;
-  for (int64_t i = 0; i < m; ++i) pairs += touched[(size_t)i];  // (row, phase) pieces in split
+  // split pipeline shape: pieces (row, phase) beyond each row's first one are accumulated
+  // into C (a read-modify-write of the row), with acc_nnz nonzeros among them
+  int64_t local_nnz = 0, acc_pieces = 0, acc_nnz = 0;
+  for (int64_t i = 0; i < m; ++i) {
+    if (touched[(size_t)i] > 1) acc_pieces += touched[(size_t)i] - 1;
+    for (int64_t j = a->indptr[i]; j < a->indptr[i + 1]; ++j) {
+      const int32_t k = (r->remap[(size_t)(a->indices[j] / cpt)] - me + P) % P;
+      local_nnz += k == 0;
+      acc_nnz += k != first[(size_t)i];
+    }
+  }
   // AUTO: split only when whole rows would leave most of the work behind the fetches, the
-  // owned tiles hold enough work (>= 30 %) to hide them, and a row's piece per phase is long
-  // (>= 12 nonzeros): every extra piece costs a read-modify-write of its C row. Measured on
-  // B200: uniform 32/row at P = 2 (50 % local, 16 per piece) +10 % split; R-MAT at P = 2
-  // (16 % local) and P = 4 (short pieces on the low-degree ranks) slower split; the
-  // stencil is rows-bound.
+  // owned tiles hold enough work (>= 30 %) to hide them, and the accumulated pieces are long
+  // (>= 12 nonzeros each). Measured on B200: uniform 32/row at P = 2 (50 % local, 16 per
+  // accumulated piece) +10 % split; R-MAT at P = 2 (the hub rank 16 % local; the other 86 %
+  // local but 8.7 per accumulated piece) and P = 4 (8.4) slower split; the stencil is
+  // rows-bound.
   if (pipeline == DSP_PIPELINE_AUTO)
-    pipeline = 2 * rows_phase0_nnz < a->nnz && 10 * local_nnz >= 3 * a->nnz && a->nnz >= 12 * pairs
+    pipeline = 2 * rows_phase0_nnz < a->nnz && 10 * local_nnz >= 3 * a->nnz && acc_pieces > 0 &&
+                       acc_nnz >= 12 * acc_pieces
                    ? DSP_PIPELINE_SPLIT
                    : DSP_PIPELINE_ROWS;
   if (P == 1 || P > 64) pipeline = DSP_PIPELINE_ROWS;

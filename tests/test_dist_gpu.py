@@ -176,8 +176,8 @@ def test_group_split_pipeline_widths(gpu, rmat12, dims):
 
 def _auto_pipeline(g, p, A):
     """The AUTO rule restated: split when whole rows would leave most nonzeros behind the
-    fetches (rows-pipeline phase 0 < 1/2), the owned tiles hold >= 30 % of them and a row's
-    piece per phase averages >= 12 nonzeros."""
+    fetches (rows-pipeline phase 0 < 1/2), the owned tiles hold >= 30 % of them and the
+    pieces accumulated after a row's first phase average >= 12 nonzeros."""
     lb, ub = g.bounds[p]
     ip = np.asarray(A.indptr[lb:ub + 1]) - A.indptr[lb]
     cols = np.asarray(A.indices[A.indptr[lb]:A.indptr[ub]])
@@ -188,8 +188,11 @@ def _auto_pipeline(g, p, A):
     phase0 = int(np.diff(ip)[last == 0].sum())
     local = int((pos == 0).sum())
     nnz = int(ip[-1])
-    pairs = np.unique(rowid.astype(np.int64) * len(g.ranks) + pos).size
-    return 2 if (2 * phase0 < nnz and 10 * local >= 3 * nnz and nnz >= 12 * pairs) else 1
+    first = np.full(ub - lb, len(g.ranks))
+    np.minimum.at(first, rowid, pos)
+    acc_nnz = int((pos != first[rowid]).sum())
+    acc_pieces = np.unique(rowid.astype(np.int64) * len(g.ranks) + pos).size - int((np.diff(ip) > 0).sum())
+    return 2 if (2 * phase0 < nnz and 10 * local >= 3 * nnz and acc_pieces > 0 and acc_nnz >= 12 * acc_pieces) else 1
 
 
 def test_pipeline_auto_choice(gpu, rmat12):
