@@ -486,6 +486,16 @@ SpmmShape spmm_shape(int N, int variant, const float *B, int64_t ldb, const floa
     if (forced_lpr > 0) lpr = forced_lpr;
     int vpl = 1;
     while (lpr * vpl < nv && vpl < max_vpl) vpl <<= 1;
+    // DSP_SPMM_COLS caps the columns one block covers (more column chunks on blockIdx.y):
+    // a smaller B-row slice per block for L1 reuse on banded matrices (sweeps)
+    static const int forced_cols = [] {
+      const char *e = getenv("DSP_SPMM_COLS");
+      return e ? atoi(e) : 0;
+    }();
+    if (forced_cols > 0) {
+      while (lpr * vpl * s.W > forced_cols && vpl > 1) vpl >>= 1;
+      while (lpr * vpl * s.W > forced_cols && lpr > 1) lpr >>= 1;
+    }
     if (!shape_supported(s.W, lpr, vpl)) {  // out-of-table request: one warp per row
       lpr = nv <= 32 ? 1 : 32;
       while (lpr < nv && lpr < 32) lpr <<= 1;
