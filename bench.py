@@ -387,41 +387,52 @@ def main(argv=None):
     if not a.no_e2e and not a.profile:
         Bh = torch.empty((M, a.dims), dtype=torch.float32, pin_memory=True)
         d.dense_b(M, a.dims, a.seed + 1, out=Bh.numpy())
-        Ch = torch.empty((max(ub - lb, 1), a.dims), dtype=torch.float32, pin_memory=True)
         # Steps back to back as an application runs them: B of step i+1 goes up (H2D
         # stream) while C of step i comes down (D2H stream); each step waits for its B and
         # for the previous C to have left the device, each upload for the previous step's
-        # reads of B. Timed from the first upload to the last download of the K steps.
+        # reads of B. On one GPU a second rank object (when memory allows) double-buffers
+        # B and C, so the SpMM of step i+1 also overlaps the download of step i. Timed from
+        # the first upload to the last download of the K steps.
+        slots = [R]
+        if comm is None:
+            free, _ = torch.cuda.mem_get_info(dev)
+            if 4 * (M + (ub - lb)) * a.dims * 4 < free:
+                slots.append(make_rank(local, rank, world, local_rank, a.dims, M, lb, tiling, plan, a.comm_type,
+                                       a.platform, a.fetch_streams, fetch_scope=a.fetch_scope, pipeline=a.pipeline))
+        Chs = [torch.empty((max(ub - lb, 1), a.dims), dtype=torch.float32, pin_memory=True) for _ in slots]
         s_up, s_dn = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
 
         def e2e_run(n):
-            ev_comp = ev_dn = None
+            ev_comp, ev_dn = [None] * len(slots), [None] * len(slots)
+            last = None
             t0 = torch.cuda.Event(enable_timing=True)
             t1 = torch.cuda.Event(enable_timing=True)
             t0.record(s_up)
-            for _ in range(n):
-                if ev_comp is not None:
-                    s_up.wait_event(ev_comp)  # B is free once the previous step's SpMM is done
-                    if comm is not None:  # ... on every rank: peers read this rank's tiles
-                        ev_comp.synchronize()
-                        comm.barrier()
-                R.upload_b_ptr(Bh.data_ptr(), s_up.cuda_stream)
+            for i in range(n):
+                k = i % len(slots)
+                X = slots[k]
+                if ev_comp[k] is not None:
+                    s_up.wait_event(ev_comp[k])  # X's B is free once its previous SpMM is done
+                if comm is not None and last is not None:  # ... on every rank: peers read its tiles
+                    last.synchronize()
+                    comm.barrier()
+                X.upload_b_ptr(Bh.data_ptr(), s_up.cuda_stream)
                 ev_up = torch.cuda.Event()
                 ev_up.record(s_up)
                 if comm is not None:  # peers read this rank's tiles only after every upload landed
                     ev_up.synchronize()
                     comm.barrier()
                 s.wait_event(ev_up)
-                if ev_dn is not None:
-                    s.wait_event(ev_dn)  # C is free once the previous download is done
-                R.step(s.cuda_stream)
-                ev_comp = torch.cuda.Event()
-                ev_comp.record(s)
-                s_dn.wait_event(ev_comp)
+                if ev_dn[k] is not None:
+                    s.wait_event(ev_dn[k])  # X's C is free once its previous download is done
+                X.step(s.cuda_stream)
+                ev_comp[k] = last = torch.cuda.Event()
+                ev_comp[k].record(s)
+                s_dn.wait_event(ev_comp[k])
                 if ub > lb:
-                    R.download_c_ptr(Ch.data_ptr(), s_dn.cuda_stream)
-                ev_dn = torch.cuda.Event()
-                ev_dn.record(s_dn)
+                    X.download_c_ptr(Chs[k].data_ptr(), s_dn.cuda_stream)
+                ev_dn[k] = torch.cuda.Event()
+                ev_dn[k].record(s_dn)
             t1.record(s_dn)
             t1.synchronize()
             if comm is not None:
@@ -429,7 +440,11 @@ def main(argv=None):
             return t0.elapsed_time(t1) / n
 
         e2e_run(max(a.warmup, 1))
-        t_e2e = e2e_run(max(a.steps, 1))
+        n_e2e = max(a.steps, 1)
+        t_e2e = e2e_run(n_e2e)
+        Ch = Chs[(n_e2e - 1) % len(slots)]
+        for X in slots[1:]:
+            X.close()
         if comm is not None:
             t_e2e = comm.allreduce_max(t_e2e)
         # spot check of the result against the oracle on a few rows of this rank
@@ -448,7 +463,8 @@ def main(argv=None):
         e2e = {"value": round(2.0 * nnz * a.dims / (t_e2e * 1e-3) / 1e9, 3), "unit": UNIT,
                "ms_per_step": round(t_e2e, 4), "h2d_bytes_per_step": st["owned_rows"] * a.dims * 4,
                "d2h_bytes_per_step": (ub - lb) * a.dims * 4,
-               "overlap": "H2D of step i+1 with D2H of step i (pinned host buffers, separate streams)",
+               "overlap": "H2D of step i+1 with D2H of step i (pinned host buffers, separate streams)"
+                          + ("; B and C double-buffered (two rank objects), SpMM overlaps both" if len(slots) > 1 else ""),
                "check": {"rows": int(rows.size), "worst_err_over_tol": round(worst, 4), "ok": bool(ok)}}
 
     cpu = None

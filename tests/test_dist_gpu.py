@@ -272,7 +272,8 @@ print(int(ok and np.isfinite(C).all()), rep.traffic_intra, rep.fetched_bytes)
 
 
 def test_dsp_run_partition_and_fetch_scope_env(gpu):
-    """The CLI pipeline's opt-in extensions (DSP_PARTITION=balanced, DSP_FETCH_SCOPE=rank):
+    """The CLI pipeline's opt-in extensions (DSP_PARTITION=balanced, DSP_FETCH_SCOPE=rank,
+    DSP_PIPELINE=split):
     same C as the oracle, and no more fetched bytes than the reference-semantics run."""
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
@@ -289,6 +290,7 @@ def test_dsp_run_partition_and_fetch_scope_env(gpu):
     _, f_rank = run(DSP_FETCH_SCOPE="rank")
     assert f_rank <= f_ref
     run(DSP_PARTITION="balanced", DSP_FETCH_SCOPE="rank")
+    run(DSP_PARTITION="balanced", DSP_FETCH_SCOPE="rank", DSP_PIPELINE="split")
 
 
 def test_cli_report_format(gpu, tmp_path):
