@@ -187,3 +187,20 @@ def test_reference_run_mode_b_all_ones(gpu):
     C = plan(torch.ones((A.num_cols, 128), device="cuda")).cpu().numpy()
     rs = np.add.reduceat(A.values.astype(np.float64), A.indptr[:-1])
     assert np.allclose(C, rs[:, None], rtol=0, atol=1e-5 * 52)
+
+
+@pytest.mark.parametrize("kind,kw,N", [("rmat", dict(scale=13), 128), ("stencil27", dict(n=20), 64),
+                                       ("uniform", dict(rows=8192, nnz_per_row=24), 256)])
+def test_agrees_with_cusparse(gpu, kind, kw, N):
+    """The reference's arithmetic is cusparseSpMM (src/dist_spmm_node.cu:354-385); torch's
+    sparse CSR product runs cuSPARSE on the same fp32 inputs. Both sit within the fp32
+    tolerance of the exact product, so they agree within twice that (cuSPARSE is used here
+    only as a checker)."""
+    import torch
+    A = d.make_matrix(kind, seed=12, **kw)
+    B, C, _ = _run(A, N, seed=13)
+    At = torch.sparse_csr_tensor(torch.from_numpy(A.indptr), torch.from_numpy(A.indices),
+                                 torch.from_numpy(A.values), size=(A.num_rows, A.num_cols)).cuda()
+    Cs = (At @ torch.from_numpy(B).cuda()).cpu().numpy()
+    _, ab = oracle.spmm_f64(A.indptr, A.indices, A.values, B)
+    assert np.all(np.abs(C - Cs) <= 2 * RTOL * ab + 1e-30), float(np.max(np.abs(C - Cs) / (ab + 1e-30)))
