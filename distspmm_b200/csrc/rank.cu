@@ -93,8 +93,9 @@ struct dsp_rank {
   std::vector<int64_t> owned;  // owned tiles
 
   cudaStream_t compute = nullptr;
+  cudaStream_t side = nullptr;  // zero fill of the empty rows, beside the phases
   std::vector<cudaStream_t> fstreams;
-  cudaEvent_t ev_start = nullptr, ev_c0 = nullptr, ev_c1 = nullptr;
+  cudaEvent_t ev_start = nullptr, ev_c0 = nullptr, ev_c1 = nullptr, ev_zero = nullptr;
   std::vector<cudaEvent_t> ev_fetch, ev_fetch_begin, ev_seg_begin, ev_seg_end;  // per peer / segment
   std::vector<bool> fetch_ran, seg_ran;                                         // last step
   dsp_rank_stats stats{};
@@ -339,7 +340,8 @@ extern "C" int dsp_rank_create(const dsp_rank_desc *d, dsp_rank **out) {
     return bail(fail(DSP_ERR_NOMEM, "scratch: %s", cudaGetErrorString(e)));
   int lo = 0, hi = 0;
   cudaDeviceGetStreamPriorityRange(&lo, &hi);
-  if ((e = cudaStreamCreateWithPriority(&r->compute, cudaStreamNonBlocking, lo)) != cudaSuccess)
+  if ((e = cudaStreamCreateWithPriority(&r->compute, cudaStreamNonBlocking, lo)) != cudaSuccess ||
+      (e = cudaStreamCreateWithPriority(&r->side, cudaStreamNonBlocking, hi)) != cudaSuccess)
     return bail(fail(DSP_ERR_CUDA, "stream: %s", cudaGetErrorString(e)));
   for (int i = 0; i < (r->P > 1 ? r->n_streams : 0); ++i) {
     cudaStream_t s;
@@ -348,7 +350,8 @@ extern "C" int dsp_rank_create(const dsp_rank_desc *d, dsp_rank **out) {
     r->fstreams.push_back(s);
   }
   if (cudaEventCreate(&r->ev_start) != cudaSuccess || cudaEventCreate(&r->ev_c0) != cudaSuccess ||
-      cudaEventCreate(&r->ev_c1) != cudaSuccess)
+      cudaEventCreate(&r->ev_c1) != cudaSuccess ||
+      cudaEventCreateWithFlags(&r->ev_zero, cudaEventDisableTiming) != cudaSuccess)
     return bail(fail(DSP_ERR_CUDA, "event create failed"));
   for (auto *v : {&r->ev_fetch, &r->ev_fetch_begin, &r->ev_seg_begin, &r->ev_seg_end}) {
     v->assign((size_t)r->P, nullptr);
@@ -394,6 +397,7 @@ extern "C" void dsp_rank_destroy(dsp_rank *r) {
   if (!r) return;
   DeviceGuard g(r->device);
   if (r->compute) cudaStreamSynchronize(r->compute);
+  if (r->side) cudaStreamSynchronize(r->side);
   for (auto s : r->fstreams) cudaStreamSynchronize(s);
   for (int p = 0; p < r->P; ++p)
     if (r->peer_ipc[(size_t)p] && r->peer_B[(size_t)p]) cudaIpcCloseMemHandle((void *)r->peer_B[(size_t)p]);
@@ -408,7 +412,8 @@ extern "C" void dsp_rank_destroy(dsp_rank *r) {
   if (r->d_err) cudaFree(r->d_err);
   for (auto s : r->fstreams) cudaStreamDestroy(s);
   if (r->compute) cudaStreamDestroy(r->compute);
-  for (auto ev : {r->ev_start, r->ev_c0, r->ev_c1})
+  if (r->side) cudaStreamDestroy(r->side);
+  for (auto ev : {r->ev_start, r->ev_c0, r->ev_c1, r->ev_zero})
     if (ev) cudaEventDestroy(ev);
   for (auto *v : {&r->ev_fetch, &r->ev_fetch_begin, &r->ev_seg_begin, &r->ev_seg_end})
     for (auto ev : *v)
@@ -552,11 +557,15 @@ extern "C" int dsp_rank_step(dsp_rank *r, void *stream_v) {
     DSP_CUDA(cudaEventRecord(r->ev_fetch[(size_t)k], fs));
     has_fetch[(size_t)k] = true;
   }
-  // compute: empty rows, then phase k once the fetches of ring positions 1..k landed; every
-  // row of C is written once (no accumulation)
+  // compute: phase k once the fetches of ring positions 1..k landed; the empty rows (other
+  // rows of C) are zero-filled beside them on the side stream
   DSP_CUDA(cudaEventRecord(r->ev_c0, r->compute));
-  int rc = launch_zero_rows(r->C, r->dims, r->d_empty, r->n_empty, r->dims, r->compute);
-  if (rc) return rc;
+  int rc;
+  if (r->n_empty) {
+    DSP_CUDA(cudaStreamWaitEvent(r->side, r->ev_c0, 0));
+    if ((rc = launch_zero_rows(r->C, r->dims, r->d_empty, r->n_empty, r->dims, r->side))) return rc;
+    DSP_CUDA(cudaEventRecord(r->ev_zero, r->side));
+  }
   r->seg_ran.assign((size_t)r->P, false);
   int waited = 0;
   for (int k = 0; k < r->P; ++k) {
@@ -575,6 +584,7 @@ extern "C" int dsp_rank_step(dsp_rank *r, void *stream_v) {
     r->seg_ran[(size_t)k] = true;
   }
   r->fetch_ran = has_fetch;
+  if (r->n_empty) DSP_CUDA(cudaStreamWaitEvent(r->compute, r->ev_zero, 0));
   DSP_CUDA(cudaEventRecord(r->ev_c1, r->compute));
   for (int k = 1; k < r->P; ++k)
     if (has_fetch[(size_t)k]) DSP_CUDA(cudaStreamWaitEvent(stream, r->ev_fetch[(size_t)k], 0));
