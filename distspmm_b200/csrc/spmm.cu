@@ -565,14 +565,17 @@ int launch_fill_const(float *B, int64_t n, float v, cudaStream_t stream) {
 
 // ------------------------------------------------------------------ device operand
 
-// Chunk length for an nnz-split operand: about default_chunk_nnz, adjusted so the chunks
-// fill a whole number of waves of resident lane groups (SMs x blocks per SM x groups per
-// block of the kernel a 32-byte aligned launch at `dims` picks). Every chunk holds the same
-// number of nonzeros, so a partial last wave would leave SMs idle while it drains: at
-// R-MAT 20 on 4 ranks a phase held 1.44 waves.
+// Chunk length for an nnz-split operand: about twice default_chunk_nnz (~64K multiply-adds),
+// adjusted so the chunks fill a whole number (>= 2) of waves of resident lane groups (SMs x
+// blocks per SM x groups per block of the kernel a 32-byte aligned launch at `dims` picks).
+// Every chunk holds the same number of nonzeros, so a partial last wave would leave SMs
+// idle while it drains (a rank's phase at R-MAT 20 on 4 ranks held 1.44 waves). Measured at
+// R-MAT 20, N = 128, one GPU (waves: GFLOPS): 1: 5531, 2: 5785, 3: 5664, 4: 5786, 5: 5543,
+// 7: 5458, 10: 5503, 14: 5428 — fewer, longer chunks cut fewer rows (less fixup) as long
+// as dynamic scheduling over a few waves absorbs the chunks' uneven cache behaviour.
 int64_t wave_chunk_nnz(int device, int dims, int64_t nnz) {
-  const int64_t c = default_chunk_nnz(dims, nnz);
-  if (getenv("DSP_SPMM_CHUNK") || nnz <= 0) return c;
+  const int64_t c = 2 * default_chunk_nnz(dims, nnz);
+  if (getenv("DSP_SPMM_CHUNK") || nnz <= 0) return default_chunk_nnz(dims, nnz);
   const float *aligned_ptr = reinterpret_cast<const float *>(uintptr_t(256));
   const int ld = (dims + 7) & ~7;
   const SpmmShape sh = spmm_shape(dims, kNnzSplit, aligned_ptr, ld, aligned_ptr, ld);
@@ -585,7 +588,7 @@ int64_t wave_chunk_nnz(int device, int dims, int64_t nnz) {
     return c;
   }
   const int64_t resident = (int64_t)sms * per_sm * (kSpmmThreads / sh.LPR) / std::max(sh.chunks, 1);
-  const int64_t waves = std::max<int64_t>(1, (nnz + c * resident - 1) / (c * resident));
+  const int64_t waves = std::max<int64_t>(2, (nnz + c * resident - 1) / (c * resident));
   return std::max<int64_t>(8, (nnz + waves * resident - 1) / (waves * resident));
 }
 
