@@ -19,7 +19,7 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, out_dir, task_dist):
+def _worker(rank, world, port, out_dir, task_dist, partition="rows"):
     import datetime
 
     import torch.distributed as dist
@@ -31,12 +31,15 @@ def _worker(rank, world, port, out_dir, task_dist):
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=60))
     A = d.gen_rmat(11, seed=3)
-    lb, ub = planner.partition_bounds(A.num_rows, world, rank)
+    lb, ub = planner.bounds(A, world, rank, partition)
     local = planner.partition(A, lb, ub)
     comm = TorchComm()
     mine, plan = distributed_plan(comm, local, n_rolls=4, task_dist=task_dist)
+    from distspmm_b200.dist import fetch_view
+    own = fetch_view(plan, mine, "rank")  # per-rank fetch lists: this rank's own tiling
     np.savez(os.path.join(out_dir, f"r{rank}.npz"), remap=plan.remap, n_col=plan.n_col, offsets=plan.offsets,
-             merged=plan.merged, demand=plan.demand)
+             merged=plan.merged, demand=plan.demand, bounds=np.array([lb, ub]), own_n_col=own.n_col,
+             own_merged=own.merged)
     assert comm.allreduce_max(float(rank)) == world - 1
     assert comm.allreduce_sum_i64(rank + 1) == world * (world + 1) // 2
     hs = comm.allgather_bytes(bytes([rank] * 64))
@@ -45,21 +48,24 @@ def _worker(rank, world, port, out_dir, task_dist):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,task_dist", [(2, 2), (3, 2), (2, 0)])
-def test_distributed_plan_matches_in_process(world, task_dist):
+@pytest.mark.parametrize("world,task_dist,partition", [(2, 2, "rows"), (3, 2, "rows"), (2, 0, "rows"),
+                                                       (3, 2, "balanced")])
+def test_distributed_plan_matches_in_process(world, task_dist, partition):
     import distspmm_b200 as d
     from distspmm_b200 import planner
     from distspmm_b200.dist import global_plan
     with tempfile.TemporaryDirectory() as tmp:
-        mp.start_processes(_worker, args=(world, _free_port(), tmp, task_dist), nprocs=world, start_method="spawn",
-                           join=True)
+        mp.start_processes(_worker, args=(world, _free_port(), tmp, task_dist, partition), nprocs=world,
+                           start_method="spawn", join=True)
         A = d.gen_rmat(11, seed=3)
         T = world * 4
-        tl = [planner.tile(planner.partition(A, *planner.partition_bounds(A.num_rows, world, p)), T)
-              for p in range(world)]
+        bnd = [planner.bounds(A, world, p, partition) for p in range(world)]
+        tl = [planner.tile(planner.partition(A, *b), T) for b in bnd]
         ref = global_plan(tl, task_dist, 4)
         for r in range(world):
             z = np.load(os.path.join(tmp, f"r{r}.npz"))
+            assert tuple(z["bounds"]) == bnd[r]  # every rank derives the same row ranges
+            assert np.array_equal(z["own_n_col"], tl[r].n_col) and np.array_equal(z["own_merged"], tl[r].needed)
             assert np.array_equal(z["remap"], ref.remap)
             assert np.array_equal(z["n_col"], ref.n_col)
             assert np.array_equal(z["offsets"], ref.offsets)
