@@ -25,6 +25,7 @@ implementation of the path: its SpMM is cuSPARSE) with all host threads, on rank
 from __future__ import annotations
 
 import argparse
+import contextlib
 import csv
 import datetime
 import io
@@ -76,6 +77,20 @@ def parse_args(argv=None):
     ap.add_argument("--profile", action="store_true",
                     help="short run for a profiler: warmup + steps only, no e2e / CPU baseline / clocks")
     return ap.parse_args(argv)
+
+
+@contextlib.contextmanager
+def stdout_to_stderr():
+    """Point file descriptor 1 at stderr for the duration (output of native libraries too)."""
+    sys.stdout.flush()
+    saved = os.dup(1)
+    os.dup2(2, 1)
+    try:
+        yield
+    finally:
+        sys.stdout.flush()
+        os.dup2(saved, 1)
+        os.close(saved)
 
 
 def env_rank():
@@ -298,9 +313,13 @@ def main(argv=None):
     comm = None
     if world > 1:
         import torch.distributed as dist
-        os.environ.setdefault("NCCL_DEBUG", "WARN")  # keep rank 0's stdout to the one JSON line
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
-        comm = TorchComm()
+        os.environ.setdefault("NCCL_DEBUG", "WARN")
+        # keep stdout to the one JSON line: the NCCL communicator set-up (eager, with
+        # device_id) may print a version banner on file descriptor 1; send it to stderr
+        with stdout_to_stderr():
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+            comm = TorchComm()
+            comm.barrier()
 
     # every rank builds the whole matrix (the reference: every rank reads the whole file)
     A = make_workload(a)
