@@ -6,6 +6,8 @@ Layers
   bin/dist_spmm_node        reference-compatible CLI
   matrix / planner / spmm / dist   Python face of the C ABI (ctypes; torch only supplies
                             device memory, streams and torch.distributed)
+  comm_test / fit_comm_model       the bulk-vs-sparse fetch microbenchmark and the
+                            selector-model fit (command lines of the reference's tools)
 """
 from ._lib import DspError, lib
 from .matrix import Csr, dense_b, gen_rmat, gen_stencil27, gen_uniform, load_from_csr, load_rows, make_matrix, save_csr
@@ -24,7 +26,7 @@ def __getattr__(name):
         from .spmm import SpmmPlan
         return SpmmPlan
     if name in ("Rank", "build_local_group", "TorchComm", "distributed_plan", "connect_peers", "make_rank",
-                "global_plan"):
+                "global_plan", "fetch_view"):
         from . import dist
         return getattr(dist, name)
     raise AttributeError(name)
