@@ -10,12 +10,12 @@ Layers
                             selector-model fit (command lines of the reference's tools)
 """
 from ._lib import DspError, lib
-from .matrix import Csr, dense_b, gen_rmat, gen_stencil27, gen_uniform, load_from_csr, load_rows, make_matrix, save_csr
+from .matrix import Csr, dense_b, dense_b_rows, gen_rmat, gen_stencil27, gen_uniform, load_from_csr, load_rows, make_matrix, save_csr
 from . import planner
 from .planner import hierarchical_iterative_refinement_allocation
 
 __all__ = [
-    "DspError", "lib", "Csr", "dense_b", "gen_rmat", "gen_stencil27", "gen_uniform", "load_from_csr", "load_rows",
+    "DspError", "lib", "Csr", "dense_b", "dense_b_rows", "gen_rmat", "gen_stencil27", "gen_uniform", "load_from_csr", "load_rows",
     "make_matrix", "save_csr", "planner", "hierarchical_iterative_refinement_allocation",
 ]
 

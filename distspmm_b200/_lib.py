@@ -76,7 +76,8 @@ class dsp_report(ctypes.Structure):
     _fields_ = [("stage_ms", c_f64 * 8), ("hsdma_ms", c_f64), ("avg_ms", c_f64), ("min_ms", c_f64),
                 ("median_ms", c_f64), ("reps_counted", c_int), ("traffic_intra", c_i64),
                 ("traffic_inter", c_i64), ("fetched_bytes", c_i64), ("mem_gb", c_f64),
-                ("gflops", c_f64), ("nnz", c_i64), ("M", c_i64), ("T", c_int), ("remap", c_i32 * 4096)]
+                ("gflops", c_f64), ("nnz", c_i64), ("M", c_i64), ("T", c_int), ("remap", c_i32 * 4096),
+                ("row_lb", c_i64), ("row_ub", c_i64)]
 
 
 # name -> (restype, argtypes); every status-returning function is checked by call().
@@ -87,6 +88,7 @@ PROTOTYPES = {
     "dsp_csr_load": (c_int, [ctypes.c_char_p, P(dsp_csr)]),
     "dsp_csr_load_rows": (c_int, [ctypes.c_char_p, c_i64, c_i64, P(dsp_csr)]),
     "dsp_csr_save": (c_int, [ctypes.c_char_p, P(dsp_csr)]),
+    "dsp_csr_read_indptr": (c_int, [ctypes.c_char_p, P(c_i64), P(c_i64)]),
     "dsp_csr_alloc": (c_int, [c_i64, c_i64, c_i64, P(dsp_csr)]),
     "dsp_csr_free": (None, [P(dsp_csr)]),
     "dsp_csr_validate": (c_int, [P(dsp_csr)]),
@@ -94,6 +96,7 @@ PROTOTYPES = {
     "dsp_gen_stencil27": (c_int, [c_i64, c_u64, P(dsp_csr)]),
     "dsp_gen_uniform": (c_int, [c_i64, c_i64, c_u64, P(dsp_csr)]),
     "dsp_fill_dense_host": (c_int, [P(c_f32), c_i64, c_i64, c_i64, c_i64, c_u64]),
+    "dsp_fill_dense_rows_host": (c_int, [P(c_f32), P(c_i64), c_i64, c_i64, c_i64, c_u64]),
     "dsp_partition_bounds": (c_int, [c_i64, c_int, c_int, P(c_i64), P(c_i64)]),
     "dsp_partition_bounds_balanced": (c_int, [P(c_i64), c_i64, c_int, c_int, P(c_i64), P(c_i64)]),
     "dsp_partition": (c_int, [P(dsp_csr), c_i64, c_i64, P(dsp_csr)]),
@@ -130,6 +133,7 @@ PROTOTYPES = {
     "dsp_rank_set_peer": (c_int, [c_vp, c_int, c_vp, c_int]),
     "dsp_rank_fill_b": (c_int, [c_vp, c_u64, c_vp]),
     "dsp_rank_upload_b": (c_int, [c_vp, c_vp, c_vp]),
+    "dsp_rank_upload_b_owned": (c_int, [c_vp, c_vp, c_vp]),
     "dsp_rank_poison_remote": (c_int, [c_vp, c_vp]),
     "dsp_rank_step": (c_int, [c_vp, c_vp]),
     "dsp_rank_check_error": (c_int, [c_vp]),
@@ -140,6 +144,11 @@ PROTOTYPES = {
     "dsp_rank_last_compute_ms": (c_int, [c_vp, P(c_f32)]),
     "dsp_rank_last_timeline": (c_int, [c_vp, P(c_f32), c_int]),
     "dsp_run": (c_int, [P(dsp_args), P(dsp_report)]),
+    "dsp_store_open": (c_int, [ctypes.c_char_p, c_int, c_int, c_f64, P(c_vp)]),
+    "dsp_store_allgather": (c_int, [c_vp, ctypes.c_char_p, c_vp, c_i64, c_vp, c_i64, P(c_i64)]),
+    "dsp_store_barrier": (c_int, [c_vp, ctypes.c_char_p]),
+    "dsp_store_close": (None, [c_vp, c_int]),
+    "dsp_run_rank": (c_int, [P(dsp_args), c_int, c_int, c_int, c_vp, P(dsp_report)]),
 }
 
 _lib = None

@@ -33,7 +33,7 @@ CXX_FLAGS = ["-O3", "-fPIC", "-std=c++17", "-ffp-contract=off", "-pthread", "-Wa
              "-I" + os.path.join(ROOT, "include"), "-I" + os.path.join(os.path.dirname(NVCC), "..", "include")]
 
 CU_SOURCES = ["spmm.cu", "rank.cu", "fetch.cu", "setup.cu"]
-CPP_SOURCES = ["host_csr.cpp", "host_gen.cpp", "host_plan.cpp", "run.cpp"]
+CPP_SOURCES = ["host_csr.cpp", "host_gen.cpp", "host_plan.cpp", "run.cpp", "run_rank.cpp", "store.cpp"]
 HEADERS = ["common.h", "internal.h", "device.cuh"]
 CLI_SOURCES = {"dist_spmm_node": "cli_dist_spmm_node.cpp"}
 

@@ -199,6 +199,14 @@ extern "C" int dsp_csr_load_rows(const char *prefix_c, int64_t row_lb, int64_t r
   return DSP_OK;
 }
 
+extern "C" int dsp_csr_read_indptr(const char *prefix_c, int64_t *M, int64_t *indptr) {
+  DSP_TRY_ARG(prefix_c && M, "dsp_csr_read_indptr: null argument");
+  std::string prefix(prefix_c);
+  int rc = open_rows(prefix, M);
+  if (rc || !indptr) return rc;
+  return read_at(prefix + "_indptr.bin", 0, *M + 1, 8, indptr);
+}
+
 extern "C" int dsp_csr_load(const char *prefix, dsp_csr *out) {
   DSP_TRY_ARG(prefix && out, "dsp_csr_load: null argument");
   int64_t M = 0;

@@ -181,3 +181,13 @@ extern "C" int dsp_fill_dense_host(float *B, int64_t row0, int64_t rows, int64_t
   }, 256);
   return DSP_OK;
 }
+
+extern "C" int dsp_fill_dense_rows_host(float *B, const int64_t *rows, int64_t n, int64_t ld, int64_t ncols,
+                                        uint64_t seed) {
+  DSP_TRY_ARG(B && (rows || n == 0) && n >= 0 && ncols >= 0 && ld >= ncols, "dsp_fill_dense_rows_host: bad argument");
+  parallel_for(n, [&](int64_t b, int64_t e) {
+    for (int64_t i = b; i < e; ++i)
+      for (int64_t c = 0; c < ncols; ++c) B[i * ld + c] = dense_value(seed, rows[i], c);
+  }, 256);
+  return DSP_OK;
+}

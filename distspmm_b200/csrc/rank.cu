@@ -518,6 +518,21 @@ extern "C" int dsp_rank_upload_b(dsp_rank *r, const float *B_host, void *stream)
   return DSP_OK;
 }
 
+extern "C" int dsp_rank_upload_b_owned(dsp_rank *r, const float *B_owned_host, void *stream) {
+  DSP_TRY_ARG(r && B_owned_host, "dsp_rank_upload_b_owned: null argument");
+  DeviceGuard g(r->device);
+  size_t off = 0;
+  for (int64_t t : r->owned) {
+    const int64_t row0 = t * r->cpt, n = std::min<int64_t>(r->cpt, r->M - row0);
+    if (n <= 0) continue;
+    const size_t bytes = sizeof(float) * (size_t)n * r->dims;
+    DSP_CUDA(cudaMemcpyAsync(r->B + (size_t)row0 * r->dims, B_owned_host + off, bytes, cudaMemcpyHostToDevice,
+                             (cudaStream_t)stream));
+    off += (size_t)n * r->dims;
+  }
+  return DSP_OK;
+}
+
 extern "C" int dsp_rank_download_c(dsp_rank *r, float *C_host, void *stream) {
   DSP_TRY_ARG(r && C_host, "dsp_rank_download_c: null argument");
   DeviceGuard g(r->device);

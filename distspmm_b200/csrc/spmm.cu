@@ -839,15 +839,30 @@ struct CsrChunkArgs {
   int64_t rows;
 };
 
-// Last row r with indptr[r] <= p (the nonempty row holding nonzero p, 0 <= p < nnz).
-__device__ __forceinline__ int64_t row_holding(const int64_t *indptr, int64_t rows, int64_t p) {
-  int64_t lo = 0, hi = rows;  // indptr[lo] <= p < indptr[hi]
+// Last row r in [lo, rows) with indptr[r] <= p (the nonempty row holding nonzero p,
+// 0 <= p < nnz), given indptr[lo] <= p.
+__device__ __forceinline__ int64_t row_holding(const int64_t *indptr, int64_t rows, int64_t p, int64_t lo = 0) {
+  int64_t hi = rows;  // indptr[lo] <= p < indptr[hi] = nnz
   while (hi - lo > 1) {
     const int64_t mid = (lo + hi) >> 1;
     if (__ldg(indptr + mid) <= p) lo = mid;
     else hi = mid;
   }
   return lo;
+}
+
+// The row holding nonzero p > the last nonzero of `row` (p < nnz): the rows a chunk moves
+// into are usually adjacent, so step forward over a few rows before searching the rest.
+// While r is below the holder, indptr[r + 1] <= p < nnz keeps r + 1 < rows, so every load
+// is in bounds, and indptr[r] <= p holds for the search that takes over.
+__device__ __forceinline__ int64_t next_row_holding(const int64_t *indptr, int64_t rows, int64_t row, int64_t p) {
+  int64_t r = row + 1;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    if (__ldg(indptr + r + 1) > p) return r;
+    ++r;
+  }
+  return row_holding(indptr, rows, p, r);
 }
 
 template <int LPR, int VPL, int W, bool kAccum>
@@ -911,7 +926,7 @@ __global__ void __launch_bounds__(kSpmmThreads) spmm_csr_chunks_kernel(const Csr
           if (j + u < n) {
             if (p >= rend) {  // group-uniform: the chunk crosses into a later row
               flush_row<LPR, VPL, W, kAccum>(a, (int32_t)row, slot_of(rbeg, rend), col0, acc);
-              const int64_t next = row_holding(ca.indptr, ca.rows, p);
+              const int64_t next = next_row_holding(ca.indptr, ca.rows, row, p);
               if (!kAccum) zero_rows<LPR, VPL, W>(a, row + 1, next, col0);
               row = next;
               rbeg = __ldg(ca.indptr + row);
@@ -1004,14 +1019,16 @@ extern "C" int dsp_spmm_csr_f32_noalloc(const int64_t *indptr, const int64_t *in
                 N, DSP_NOALLOC_MAX_N, kNoAllocScratchBytes);
   if (rows > INT32_MAX)
     return fail(DSP_ERR_UNSUPPORTED, "dsp_spmm_csr_f32_noalloc: %lld rows exceed 2^31 - 1", (long long)rows);
-  if (N == 0 || rows == 0) return DSP_OK;
-  DSP_TRY_ARG(indptr && C && (nnz == 0 || (indices && values && B)), "dsp_spmm_csr_f32_noalloc: null argument");
+  // the scratch address first, so that a call with nothing to compute (N, rows or nnz 0)
+  // sets the device up ahead of latency-critical work or stream capture
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return fail(DSP_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
   float *slots = nullptr;
   int rc = noalloc_scratch(dev, &slots);
   if (rc) return rc;
+  if (N == 0 || rows == 0) return DSP_OK;
+  DSP_TRY_ARG(indptr && C && (nnz == 0 || (indices && values && B)), "dsp_spmm_csr_f32_noalloc: null argument");
   cudaStream_t st = (cudaStream_t)stream;
   if (nnz == 0) {
     if (accumulate) return DSP_OK;

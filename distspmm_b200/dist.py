@@ -64,6 +64,7 @@ class Rank:
         self.rank, self.world, self.device, self.dims, self.M = rank, world, device, dims, M
         self.m_local = local.num_rows
         self.m_lb = m_lb
+        self.T, self.cpt, self.remap = plan.T, plan.cpt, np.array(plan.remap, np.int32)
         self._keep = [local, plan, np.ascontiguousarray(n_slice, np.int32), np.ascontiguousarray(sparse, np.uint8)]
         c = local.to_c()
         self._keep.append(c)
@@ -121,6 +122,21 @@ class Rank:
 
     def upload_b_ptr(self, host_ptr: int, stream: int = 0) -> None:
         call("dsp_rank_upload_b", self._h, host_ptr, stream)
+
+    def upload_b_owned_ptr(self, host_ptr: int, stream: int = 0) -> None:
+        """Owned tiles only, back to back in ascending tile order (owned_rows x dims)."""
+        call("dsp_rank_upload_b_owned", self._h, host_ptr, stream)
+
+    def owned_tiles(self) -> list:
+        """(first row, rows) of every owned tile, ascending: the layout of upload_b_owned."""
+        out = []
+        for t in range(self.T):
+            if self.remap[t] == self.rank:
+                row0 = t * self.cpt
+                n = min(self.cpt, self.M - row0)
+                if n > 0:
+                    out.append((row0, n))
+        return out
 
     def step(self, stream: int = 0) -> None:
         call("dsp_rank_step", self._h, stream)

@@ -114,6 +114,15 @@ def dense_b(rows: int, ncols: int, seed: int, row0: int = 0, out: np.ndarray | N
     return B
 
 
+def dense_b_rows(rows: np.ndarray, ncols: int, seed: int) -> np.ndarray:
+    """The listed global rows of the synthetic dense B (the values dense_b gives them)."""
+    rows = np.ascontiguousarray(rows, np.int64)
+    B = np.empty((rows.size, ncols), np.float32)
+    call("dsp_fill_dense_rows_host", B.ctypes.data_as(P(c_f32)), rows.ctypes.data_as(P(c_i64)), rows.size, ncols,
+         ncols, seed)
+    return B
+
+
 def make_matrix(kind: str, seed: int = 1, **kw) -> Csr:
     """Named synthetic matrices of the benchmark configurations."""
     if kind == "rmat":

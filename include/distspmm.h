@@ -77,6 +77,11 @@ int dsp_csr_load(const char *prefix, dsp_csr *out);
  * without every rank reading the whole matrix. num_cols is the global row count. */
 int dsp_csr_load_rows(const char *prefix, int64_t row_lb, int64_t row_ub, dsp_csr *out);
 
+/* Row count M of the binary CSR at <prefix> (from the size of <prefix>_indptr.bin) and, when
+ * indptr is not NULL, the whole indptr[M+1]: what a rank needs to find its rows before it
+ * reads them with dsp_csr_load_rows (src/sparse_matrix.h:85-101 reads the same file). */
+int dsp_csr_read_indptr(const char *prefix, int64_t *M, int64_t *indptr);
+
 /* Write the three binary files in the layout of tools/gen_graph500_matrix.py:40-49. */
 int dsp_csr_save(const char *prefix, const dsp_csr *a);
 
@@ -104,6 +109,10 @@ int dsp_gen_uniform(int64_t rows, int64_t nnz_per_row, uint64_t seed, dsp_csr *o
  * counter hash of (seed, r, c), identical on host and device. ld >= ncols. */
 int dsp_fill_dense_host(float *B, int64_t row0, int64_t rows, int64_t ld, int64_t ncols,
                         uint64_t seed);
+/* The same values for the listed global rows: B[i] = row rows[i] of the synthetic B (the
+ * rows a sampled check needs, without materialising all of B). */
+int dsp_fill_dense_rows_host(float *B, const int64_t *rows, int64_t n, int64_t ld, int64_t ncols,
+                             uint64_t seed);
 
 /* ---------------------------------------------------------------- planning (host, integer) */
 /* 1-D row partition: m_local = ceil(M/P), lb = rank*m_local, ub = min(lb+m_local, M)
@@ -266,10 +275,16 @@ int dsp_spmm_f32(dsp_spmm_plan *p, const float *B, int64_t ldb, float *C, int64_
  * routine: its only scratch (partial rows of rows cut between work chunks) is a static
  * 32 MiB device array that every GPU loading the library holds until exit.
  * Limits: N <= DSP_NOALLOC_MAX_N and rows < 2^31 (DSP_ERR_UNSUPPORTED otherwise).
- * The first call on a device looks up that device's scratch address
- * (cudaGetSymbolAddress), so make it before any stream capture. All calls on a device share
- * the scratch: calls that overlap on the GPU (e.g. on two streams) race; serialise them.
- * The scratch keeps the last call's contents; no call relies on it being zero. */
+ * Set-up: the first call on a device looks up that device's scratch address
+ * (cudaGetSymbolAddress, once per device, cached for the process). Under lazy module
+ * loading that first lookup may also load the library's device code together with its
+ * 32 MiB array, which allocates and can synchronise the device. So make one call per device
+ * before any stream capture or latency-critical work; a call with N = 0 or rows = 0 does the
+ * set-up and touches no memory. The cached address belongs to the device's context
+ * at that time: do not use this entry point on a device after cudaDeviceReset.
+ * All calls on a device share the scratch: calls that overlap on the GPU (e.g. on two
+ * streams) race; serialise them. The scratch keeps the last call's contents; no call relies
+ * on it being zero. */
 #define DSP_NOALLOC_MAX_N 2048
 int dsp_spmm_csr_f32_noalloc(const int64_t *indptr, const int64_t *indices, const float *values,
                              int64_t rows, int64_t cols, int64_t nnz, const float *B, int64_t ldb,
@@ -355,6 +370,10 @@ int dsp_rank_fill_b(dsp_rank *r, uint64_t seed, void *stream);
 int dsp_rank_poison_remote(dsp_rank *r, void *stream);
 /* Copy the owned tiles of a full host B (M x dims, row-major) into the device B. */
 int dsp_rank_upload_b(dsp_rank *r, const float *B_host, void *stream);
+/* Same from a host buffer holding only the owned tiles, back to back in ascending tile
+ * order (owned_rows x dims, dsp_rank_stats.owned_rows): a rank's share of B without a full
+ * M x dims host copy. */
+int dsp_rank_upload_b_owned(dsp_rank *r, const float *B_owned_host, void *stream);
 /* One distributed SpMM: fetch the needed remote rows (bulk copy-engine copies and
  * sparse NVLink gather kernels on the fetch streams) while the SpMM kernels run segment
  * by segment on the compute stream; C = A_local * B. Ordered after prior work on
@@ -419,9 +438,41 @@ typedef struct dsp_report {
   int64_t nnz, M;
   int T;
   int32_t remap[4096];
+  int64_t row_lb, row_ub;               /* dsp_run_rank: this rank's rows           */
 } dsp_report;
 
 int dsp_run(const dsp_args *args, dsp_report *report);
+
+/* ---------------------------------------------------------------- one process per rank */
+/* Host collectives for ranks launched as separate processes on one node, in place of the
+ * reference's MPI (MPI_Gather/Bcast of src/utils.h:358-437, MPI_Allgather(v) of
+ * src/utils.h:439-547, MPI_Allreduce of src/dist_spmm_node.cu:401-409). The ranks meet in a
+ * directory every process of the job can reach (tmpfs); each value is one file written
+ * atomically; every wait is bounded by timeout_s (<= 0: 300 s) and then fails with
+ * DSP_ERR_TIMEOUT, so a rank that died or never started is reported instead of hanging
+ * the others. Every rank makes the same calls with the same keys in the same order; a
+ * key is used once per store. */
+typedef struct dsp_store dsp_store;
+int dsp_store_open(const char *dir, int rank, int world, double timeout_s, dsp_store **out);
+/* Publish `bytes` bytes under key and collect every rank's value, rank by rank, into out
+ * (capacity out_cap; NULL to collect sizes only); sizes[world] receives each rank's size
+ * (may be NULL). */
+int dsp_store_allgather(dsp_store *s, const char *key, const void *data, int64_t bytes, void *out,
+                        int64_t out_cap, int64_t *sizes);
+int dsp_store_barrier(dsp_store *s, const char *key);
+/* remove_dir: after every rank's last collective, rank 0 deletes the directory (every
+ * rank must close with the same flag). */
+void dsp_store_close(dsp_store *s, int remove_dir);
+
+/* Rank `rank` of `world` of the dist_spmm_node program (src/dist_spmm_node.cu:20-444) when
+ * every rank is its own process on its own GPU (`device`), as under `mpirun -np P`
+ * (src/utils.h:176-237 binds a rank to the GPU of its node-local rank). args->world and
+ * args->devices are ignored; the rank reads only its own rows of args->file; peers' B
+ * buffers are opened by CUDA IPC. Every rank gets the same report (times MAX over ranks,
+ * traffic summed), plus its own row range; args->c_out, when set, receives this rank's
+ * rows of C ([row_ub - row_lb] x dims). */
+int dsp_run_rank(const dsp_args *args, int rank, int world, int device, dsp_store *store,
+                 dsp_report *report);
 
 #ifdef __cplusplus
 }

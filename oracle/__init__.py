@@ -40,11 +40,13 @@ _lib = None
 _ref = None
 
 
-def build(ref: bool = True) -> None:
-    """Compile liboracle.so (and the reference shim when the reference tree exists)."""
+def build(ref: bool = True, ref_src: str | None = None) -> None:
+    """Compile liboracle.so (and the reference shim when the reference tree exists; its
+    src/ directory is ``ref_src`` or the DSP_REFERENCE_SRC environment variable)."""
     subprocess.run(["make", "-s", "-C", _HERE, "oracle"], check=True)
-    if ref:
-        subprocess.run(["make", "-s", "-C", _HERE, "ref"], check=True)
+    src = ref_src or os.environ.get("DSP_REFERENCE_SRC")
+    if ref and src:
+        subprocess.run(["make", "-s", "-C", _HERE, "ref", f"REF_SRC={src}"], check=True)
 
 
 def _p(a, t):
@@ -134,6 +136,41 @@ def check_close(C_dev, C_ref, C_abs, rel: float = 1e-5):
     ratio = diff / bound
     worst = float(ratio.max()) if ratio.size else 0.0
     return worst <= 1.0, worst
+
+
+def sample_rows(num_rows, frac=0.01, indptr=None, min_degree=None, offset=0):
+    """Rows to check at sizes where a full CPU product is too slow: every k-th row
+    (k = 1/frac, starting at `offset`), plus every row holding more than `min_degree`
+    nonzeros when indptr is given (the hub rows of power-law matrices)."""
+    k = max(1, int(round(1.0 / frac)))
+    rows = np.arange(offset % k, num_rows, k, dtype=np.int64)
+    if indptr is not None and min_degree is not None:
+        heavy = np.nonzero(np.diff(np.asarray(indptr, np.int64)) > min_degree)[0]
+        rows = np.union1d(rows, heavy)
+    return rows
+
+
+def check_rows(indptr, indices, values, B, rows, C_rows, rel: float = 1e-5):
+    """check_close of C_rows (the device result at `rows` of a CSR) against the oracle
+    computed on those rows only. B is the dense operand, or a function returning the B
+    rows of a list of column ids (so that B never has to exist whole on the host).
+    Returns (ok, worst_ratio)."""
+    indptr = np.asarray(indptr, np.int64)
+    rows = np.asarray(rows, np.int64)
+    lens = indptr[rows + 1] - indptr[rows]
+    ip = np.zeros(rows.size + 1, np.int64)
+    np.cumsum(lens, out=ip[1:])
+    if rows.size and ip[-1] > 0:
+        starts = np.repeat(indptr[rows] - ip[:-1], lens)
+        sel = np.arange(ip[-1], dtype=np.int64) + starts
+    else:
+        sel = np.zeros(0, np.int64)
+    cols = np.asarray(indices)[sel]
+    if callable(B):
+        uniq, cols = np.unique(cols, return_inverse=True)
+        B = B(uniq) if uniq.size else np.zeros((1, np.asarray(C_rows).shape[1]), np.float32)
+    ref, ab = spmm_f64(ip, cols, np.asarray(values)[sel], B)
+    return check_close(np.asarray(C_rows), ref, ab, rel)
 
 
 # ---------------------------------------------------------------- planning

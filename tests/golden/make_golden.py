@@ -1,6 +1,6 @@
-"""Generate the golden fixtures of tests/golden/ (run here, where the reference exists).
+"""Generate the golden fixtures of tests/golden/ (run where the reference checkout exists).
 
-    python tests/golden/make_golden.py
+    DSP_REFERENCE_ROOT=<reference checkout> python tests/golden/make_golden.py
 
 Fixtures and their source of truth:
   hsdma_cases.json     remap[] from the reference's own hierarchical_iterative_refinement_
@@ -91,7 +91,8 @@ def make_thresholds():
         json.dump(res, f, indent=1)
 
 
-def make_fit(ref_root="/root/reference"):
+def make_fit(ref_root=None):
+    ref_root = ref_root or os.environ["DSP_REFERENCE_ROOT"]
     import importlib.util
     spec = importlib.util.spec_from_file_location("ref_fit", os.path.join(ref_root, "tools", "fit_comm_model.py"))
     ref = importlib.util.module_from_spec(spec)
@@ -108,7 +109,7 @@ def make_fit(ref_root="/root/reference"):
 
 if __name__ == "__main__":
     make_fit()
-    oracle.build(ref=True)
+    oracle.build(ref=True, ref_src=os.path.join(os.environ["DSP_REFERENCE_ROOT"], "src"))
     if oracle.ref_lib() is None:
         sys.exit("reference shim not available: run where the reference sources exist")
     make_hsdma()

@@ -109,3 +109,37 @@ def test_oracle_hsdma_random_vs_reference_build():
         D = rng.integers(0, 20, size=(P, P * rolls))
         node = np.repeat(np.arange(nodes), P // nodes)
         assert (oracle.hsdma(D, node, rolls) == oracle.hsdma(D, node, rolls, use_ref=True)).all()
+
+
+def test_check_rows_matches_full_product_on_the_sample():
+    """The sampled-row checker used at full benchmark sizes computes the same rows as the
+    full oracle product, and flags a planted error (planted in the oracle's output, on the
+    CPU)."""
+    import distspmm_b200 as d
+    A = d.gen_rmat(11, seed=3)
+    B = d.dense_b(A.num_cols, 24, seed=4)
+    C, _ = oracle.spmm_f64(A.indptr, A.indices, A.values, B)
+    rows = oracle.sample_rows(A.num_rows, 0.05, A.indptr, 64, offset=3)
+    assert 3 in rows and 23 in rows and (np.diff(A.indptr)[rows] > 64).sum() == (np.diff(A.indptr) > 64).sum()
+    ok, worst = oracle.check_rows(A.indptr, A.indices, A.values, B, rows, C[rows].astype(np.float32))
+    assert ok and worst < 0.1
+    bad = C[rows].astype(np.float32)
+    hub = int(np.argmax(np.diff(A.indptr)[rows]))
+    bad[hub, 5] += 1e-2
+    ok, worst = oracle.check_rows(A.indptr, A.indices, A.values, B, rows, bad)
+    assert not ok and worst > 1.0
+
+
+def test_check_rows_with_b_rows_on_demand():
+    """The checker can take B as a row source (global ids -> rows), as the benchmark does
+    at sizes where B is not materialised on the host; the result equals the full-B check."""
+    import distspmm_b200 as d
+    A = d.gen_uniform(3000, 7, seed=5)
+    B = d.dense_b(A.num_cols, 16, seed=9)
+    C, _ = oracle.spmm_f64(A.indptr, A.indices, A.values, B)
+    rows = oracle.sample_rows(A.num_rows, 0.1, offset=1)
+    full = oracle.check_rows(A.indptr, A.indices, A.values, B, rows, C[rows].astype(np.float32))
+    lazy = oracle.check_rows(A.indptr, A.indices, A.values, lambda r: d.dense_b_rows(r, 16, 9), rows,
+                             C[rows].astype(np.float32))
+    assert full[0] and lazy[0] and abs(full[1] - lazy[1]) < 1e-12
+    assert np.array_equal(d.dense_b_rows(np.array([5, 0, 2999]), 16, 9), B[[5, 0, 2999]])
