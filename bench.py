@@ -4,20 +4,29 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     torchrun --nproc-per-node N bench.py --gpus N ...      (one rank per GPU)
 
-Workload: R-MAT scale 20, edge factor 16,
-(a,b,c,d) = (.57,.19,.19,.05), symmetrised, deduplicated, no self-loops (31.4 M nnz),
-values U(0,1); dense B 1,048,576 x 128 fp32 U(-1,1); 1-D row partition over the ranks,
-T = 4 tiles per rank, HSDMA allocation (task_dist 2), adaptive fetch (comm_type 2).
-All inputs are seeded synthetic data generated here. The matrix is fixed as N grows
-(strong scaling, as the reference partitions one matrix).
+Workload (the largest single-GPU one): R-MAT scale 24, edge
+factor 16, (a,b,c,d) = (.57,.19,.19,.05), symmetrised, deduplicated, no self-loops
+(16,777,216 rows, ~520 M nnz), values U(0,1); dense B 16,777,216 x 128 fp32 U(-1,1);
+1-D row partition over the ranks, T = 4 tiles per rank, HSDMA allocation (task_dist 2),
+adaptive fetch (comm_type 2). Other configurations are flags (--scale 15/20, --matrix
+stencil27 | uniform, --dims). All inputs are seeded synthetic data generated here; at
+N > 1 rank 0 writes the matrix once as the reference's binary CSR files (tmpfs) and every
+rank reads only its own rows. The matrix is fixed as N grows (strong scaling, as the
+reference partitions one matrix).
 
 A step is one distributed SpMM C = A.B over the whole matrix: every rank fetches its
 needed remote B rows (copy-engine bulk copies / NVLink gather kernels) and runs its
 SpMM segments. Metric: GFLOPS = 2.nnz.dims / t, t = device time of a step (CUDA events
 on the launching stream, mean over K steps, max over ranks). L2 is flushed between steps
 (a 512 MiB write outside the timed events). `e2e` times the same steps through the C ABI
-from pinned host memory: H2D of the rank's owned B tiles, the step, D2H of its C rows, run
-back to back with the upload of step i+1 overlapping the download of step i.
+from pinned host memory: H2D of the rank's owned B tiles, the step, D2H of its C rows,
+back to back with B and C double-buffered (two rank objects) so that uploads, SpMM and
+downloads of consecutive steps overlap; at N > 1 the ranks order their uploads and
+peers' reads with stream-ordered NCCL all-reduces of one element (no host barrier per
+step). Every rank then checks a 1 % row sample of its C (plus every hub row) against the
+CPU oracle; a failed check makes the run exit non-zero. At N = 1 the line also carries
+`cusparse`: the reference's own local SpMM (cuSPARSE per-tile COO, ALG_DEFAULT, beta = 1)
+and a whole-matrix CSR cuSPARSE call, timed the same way on the same B.
 
 `--impl reference` times the CPU CSR x dense loop of the oracle (the reference has no CPU
 implementation of the path: its SpMM is cuSPARSE) with all host threads, on rank 0.
@@ -53,7 +62,7 @@ def parse_args(argv=None):
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--matrix", choices=["rmat", "stencil27", "uniform"], default="rmat",
                     help="rmat: configurations 1/2/5; stencil27: configuration 3; uniform: configuration 4")
-    ap.add_argument("--scale", type=int, default=20, help="R-MAT scale")
+    ap.add_argument("--scale", type=int, default=24, help="R-MAT scale")
     ap.add_argument("--grid", type=int, default=160, help="stencil grid edge (160 -> 4,096,000 rows)")
     ap.add_argument("--rows", type=int, default=1 << 22, help="uniform matrix rows")
     ap.add_argument("--nnz-per-row", type=int, default=32, help="uniform matrix nonzeros per row")
@@ -74,6 +83,8 @@ def parse_args(argv=None):
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-flush", action="store_true")
+    ap.add_argument("--no-cusparse", action="store_true", help="skip the cuSPARSE comparison arm (N = 1)")
+    ap.add_argument("--check-frac", type=float, default=0.01, help="fraction of each rank's rows checked")
     ap.add_argument("--profile", action="store_true",
                     help="short run for a profiler: warmup + steps only, no e2e / CPU baseline / clocks")
     return ap.parse_args(argv)
@@ -219,72 +230,85 @@ class Clocks:
                 "reasons": reasons, "samples": len(rows)}
 
 
-def cpu_spmm_baseline(A, B, budget_s=10.0, max_reps=5):
-    """Time the oracle's fp32 OpenMP CSR x dense loop (all host threads) on the full matrix,
-    or on a strided row sample when one pass would exceed the budget."""
+
+
+def hub_degree(a):
+    """Rows longer than this are always checked (R-MAT hubs, cut into pieces by the kernels)."""
+    return max(4096, 1 << max(0, a.scale - 10)) if a.matrix == "rmat" else 1 << 30
+
+
+def row_sample(indptr, target_nnz, offset=0):
+    """Every k-th row, k chosen so that the sample holds about target_nnz nonzeros, as a
+    compact CSR (indptr rebased) plus the sampled row ids."""
+    import numpy as np
+    m = indptr.size - 1
+    nnz = int(indptr[-1] - indptr[0])
+    k = max(1, -(-nnz // max(target_nnz, 1)))
+    rows = np.arange(offset % k, m, k, dtype=np.int64)
+    lens = indptr[rows + 1] - indptr[rows]
+    ip = np.zeros(rows.size + 1, np.int64)
+    np.cumsum(lens, out=ip[1:])
+    starts = np.repeat(indptr[rows] - ip[:-1], lens)
+    sel = np.arange(int(ip[-1]), dtype=np.int64) + starts
+    return k, rows, ip, sel
+
+
+def compact_b(cols, dims, seed):
+    """B rows of the distinct columns `cols` needs, and cols renumbered into them."""
+    import numpy as np
+
+    import distspmm_b200 as d
+    uniq, inv = np.unique(cols, return_inverse=True)
+    return d.dense_b_rows(uniq, dims, seed), inv.astype(np.int64)
+
+
+def cpu_spmm_baseline(A, dims, seed, budget_s=10.0, max_reps=5, target_nnz=16 << 20):
+    """Time the oracle's fp32 OpenMP CSR x dense loop (all host threads) on a strided row
+    sample of about target_nnz nonzeros (the whole matrix when it is smaller)."""
     import numpy as np
 
     import oracle
     threads = host_threads()
-    C = np.empty((A.num_rows, B.shape[1]), np.float32)
-    t0 = time.perf_counter()
-    oracle.spmm_f32(A.indptr, A.indices, A.values, B, threads=threads, out=C)
-    first = time.perf_counter() - t0
-    sample = "full matrix"
-    ip, ix, vv, nnz = A.indptr, A.indices, A.values, A.nnz
-    if first > budget_s / 2:
-        k = int(first / (budget_s / 8)) + 1
-        rows = np.arange(0, A.num_rows, k)
-        lens = np.diff(A.indptr)[rows]
-        ip = np.concatenate([[0], np.cumsum(lens)]).astype(np.int64)
-        sel = np.concatenate([np.arange(A.indptr[r], A.indptr[r + 1]) for r in rows])
-        ix, vv, nnz = A.indices[sel], A.values[sel], int(ip[-1])
-        C = np.empty((rows.size, B.shape[1]), np.float32)
-        sample = f"every {k}-th row ({rows.size} rows, {nnz} nnz)"
+    k, rows, ip, sel = row_sample(A.indptr, target_nnz)
+    Bc, cols = compact_b(A.indices[sel], dims, seed)
+    vals = A.values[sel]
+    nnz = int(ip[-1])
+    C = np.empty((rows.size, dims), np.float32)
     times = []
     t_end = time.perf_counter() + budget_s
     while len(times) < max_reps and (not times or time.perf_counter() < t_end):
         t0 = time.perf_counter()
-        oracle.spmm_f32(ip, ix, vv, B, threads=threads, out=C)
+        oracle.spmm_f32(ip, cols, vals, Bc, threads=threads, out=C)
         times.append(time.perf_counter() - t0)
     t = statistics.median(times)
-    return {"value": round(2.0 * nnz * B.shape[1] / t / 1e9, 3), "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"{sample}, dims {B.shape[1]}, median of {len(times)} passes"}
+    sample = "full matrix" if k == 1 else f"every {k}-th row ({rows.size} rows, {nnz} nnz)"
+    return {"value": round(2.0 * nnz * dims / t / 1e9, 3), "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{sample}, dims {dims}, B rows of the sampled columns, median of {len(times)} passes"}
 
 
 def run_reference(a, rank, world):
-    """CPU arm: the oracle's fp32 OpenMP loop on rank 0 (other ranks exit without work)."""
+    """CPU arm: the oracle's fp32 OpenMP loop on rank 0 (other ranks exit without work),
+    each step one pass over a strided row sample of the workload (about 8 M nonzeros)."""
     if rank != 0:
         return 0
-    import distspmm_b200 as d
-    A = make_workload(a)
-    B = d.dense_b(A.num_cols, a.dims, seed=a.seed + 1)
     import numpy as np
 
     import oracle
+    A = make_workload(a)
     threads = host_threads()
-    C = np.empty((A.num_rows, a.dims), np.float32)
-    t0 = time.perf_counter()
-    oracle.spmm_f32(A.indptr, A.indices, A.values, B, threads=threads, out=C)
-    one = time.perf_counter() - t0
-    # bound the whole run to about two minutes
-    k = max(1, int(one * (a.steps + a.warmup) / 120.0) + 1)
-    ip, ix, vv, nnz, sample = A.indptr, A.indices, A.values, A.nnz, "full matrix"
-    if k > 1:
-        rows = np.arange(0, A.num_rows, k)
-        lens = np.diff(A.indptr)[rows]
-        ip = np.concatenate([[0], np.cumsum(lens)]).astype(np.int64)
-        sel = np.concatenate([np.arange(A.indptr[r], A.indptr[r + 1]) for r in rows])
-        ix, vv, nnz = A.indices[sel], A.values[sel], int(ip[-1])
-        C = np.empty((rows.size, a.dims), np.float32)
-        sample = f"every {k}-th row ({rows.size} rows, {nnz} nnz)"
+    k, rows, ip, sel = row_sample(A.indptr, 8 << 20)
+    Bc, cols = compact_b(A.indices[sel], a.dims, a.seed + 1)
+    vals = A.values[sel]
+    nnz = int(ip[-1])
+    C = np.empty((rows.size, a.dims), np.float32)
     for _ in range(a.warmup):
-        oracle.spmm_f32(ip, ix, vv, B, threads=threads, out=C)
+        oracle.spmm_f32(ip, cols, vals, Bc, threads=threads, out=C)
     t0 = time.perf_counter()
     for _ in range(a.steps):
-        oracle.spmm_f32(ip, ix, vv, B, threads=threads, out=C)
+        oracle.spmm_f32(ip, cols, vals, Bc, threads=threads, out=C)
     dt = (time.perf_counter() - t0) / max(a.steps, 1)
     v = 2.0 * nnz * a.dims / dt / 1e9
+    sample = "full matrix" if k == 1 else f"every {k}-th row ({rows.size} rows, {nnz} nnz)"
     line = {"metric": METRIC, "value": round(v, 3), "unit": UNIT, "n_gpus": world, "steps": a.steps,
             "warmup": a.warmup, "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
@@ -294,6 +318,110 @@ def run_reference(a, rank, world):
             "e2e": {"value": round(v, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
+
+
+def load_local(a, rank, world, comm):
+    """This rank's rows. N = 1: the generated matrix itself. N > 1: rank 0 generates the
+    matrix once and writes the reference's binary CSR files to tmpfs; every rank reads the
+    row pointer, finds its rows (planner.bounds) and reads only those (load_rows).
+    Returns (local, M, nnz, lb, ub, cleanup)."""
+    import numpy as np
+
+    import distspmm_b200 as d
+    from distspmm_b200 import planner
+    if world == 1:
+        A = make_workload(a)
+        return A, A.num_rows, A.nnz, 0, A.num_rows, None
+    import torch.distributed as dist
+    box = [None]
+    if rank == 0:
+        A = make_workload(a)
+        base = "/dev/shm" if os.path.isdir("/dev/shm") else None
+        tmp = tempfile.mkdtemp(prefix="dsp_bench_", dir=base)
+        d.save_csr(os.path.join(tmp, "A"), A)
+        del A
+        box[0] = tmp
+    dist.broadcast_object_list(box, src=0)
+    tmp = box[0]
+    prefix = os.path.join(tmp, "A")
+    ip = np.fromfile(prefix + "_indptr.bin", np.int64)
+    M = ip.size - 1
+    nnz = int(ip[-1])
+    g = d.Csr(ip, np.zeros(0, np.int64), np.zeros(0, np.float32), M, M)
+    lb, ub = planner.bounds(g, world, rank, a.partition)
+    local = d.load_rows(prefix, lb, ub)
+    comm.barrier()  # every rank has read its rows
+
+    def cleanup():
+        if rank == 0:
+            for f in os.listdir(tmp):
+                os.unlink(os.path.join(tmp, f))
+            os.rmdir(tmp)
+    return local, M, nnz, lb, ub, cleanup
+
+
+def check_c(a, local, C_rows_of, rank):
+    """Sampled check of this rank's C against the oracle: every k-th local row (k from
+    --check-frac, offset by the rank) plus every row longer than hub_degree(a). C_rows_of
+    maps local row ids to their computed rows. Returns (rows checked, worst ratio)."""
+    import distspmm_b200 as d
+    import oracle
+    rows = oracle.sample_rows(local.num_rows, a.check_frac, local.indptr, hub_degree(a), offset=rank)
+    if rows.size == 0:
+        return 0, 0.0
+    got = C_rows_of(rows)
+    _, worst = oracle.check_rows(local.indptr, local.indices, local.values,
+                                 lambda cols: d.dense_b_rows(cols, a.dims, a.seed + 1), rows, got, 1e-5)
+    return int(rows.size), float(worst)
+
+
+def cusparse_arm(a, local, M, R, flush_l2, ours_ms):
+    """The reference's local SpMM on this GPU, on R's B: cuSPARSE per-tile COO (int64,
+    ALG_DEFAULT, beta = 1 over T = n_rolls tiles; src/dist_spmm_node.cu:206-234, :354-385)
+    and a whole-matrix CSR call; CUDA events, L2 flushed before each run, mean of 5."""
+    import torch
+
+    import baseline
+    dev = torch.device("cuda", torch.cuda.current_device())
+    C = torch.empty((local.num_rows, a.dims), dtype=torch.float32, device=dev)
+    s = torch.cuda.Stream(dev)
+    arm = baseline.CusparseArm(local, M, a.n_rolls, a.dims, R.b_ptr(), C.data_ptr())
+
+    def timed(fn, pre=None, reps=5):
+        fn()
+        torch.cuda.synchronize(dev)
+        ts = []
+        for _ in range(reps):
+            flush_l2()
+            if pre:
+                with torch.cuda.stream(s):
+                    pre()
+            torch.cuda.synchronize(dev)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(s)
+            fn()
+            e1.record(s)
+            e1.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        return statistics.mean(ts)
+
+    zero = lambda: C.zero_()  # noqa: E731 — the reference zeroes C before each rep, untimed
+    t_tiles = timed(lambda: arm.run_tiles(R.b_ptr(), C.data_ptr(), s.cuda_stream), pre=zero)
+    _, w_tiles = check_c(a, local, lambda r: C[torch.from_numpy(r).to(dev)].cpu().numpy(), 0)
+    t_csr = timed(lambda: arm.run_csr(R.b_ptr(), C.data_ptr(), s.cuda_stream))
+    _, w_csr = check_c(a, local, lambda r: C[torch.from_numpy(r).to(dev)].cpu().numpy(), 0)
+    arm.close()
+    del C
+    torch.cuda.empty_cache()
+    g = lambda ms: round(2.0 * local.nnz * a.dims / (ms * 1e-3) / 1e9, 3)  # noqa: E731
+    best = min(t_tiles, t_csr)
+    return {"reference_tiles_coo": {"ms": round(t_tiles, 4), "gflops": g(t_tiles), "tiles": a.n_rolls,
+                                    "check_worst_err_over_tol": round(w_tiles, 4)},
+            "csr_whole_matrix": {"ms": round(t_csr, 4), "gflops": g(t_csr),
+                                 "check_worst_err_over_tol": round(w_csr, 4)},
+            "ours_ms": round(ours_ms, 4), "speedup_vs_best_cusparse": round(best / ours_ms, 3),
+            "how": "cusparseSpMM fp32, int64 indices, CUSPARSE_SPMM_ALG_DEFAULT; descriptors and buffers made "
+                   "once; CUDA events, L2 flushed before each of 5 runs; same B as ours"}
 
 
 def main(argv=None):
@@ -317,30 +445,33 @@ def main(argv=None):
         # keep stdout to the one JSON line: the NCCL communicator set-up (eager, with
         # device_id) may print a version banner on file descriptor 1; send it to stderr
         with stdout_to_stderr():
-            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
             comm = TorchComm()
             comm.barrier()
 
-    # every rank builds the whole matrix (the reference: every rank reads the whole file)
-    A = make_workload(a)
-    M, nnz = A.num_rows, A.nnz
-    lb, ub = planner.bounds(A, world, rank, a.partition)
-    local = planner.partition(A, lb, ub)
+    t_setup = time.perf_counter()
+    local, M, nnz, lb, ub, cleanup = load_local(a, rank, world, comm)
     if comm is None:
         tiling = planner.tile(local, a.n_rolls)
         plan = global_plan([tiling], a.task_dist, a.n_rolls)
     else:
         tiling, plan = distributed_plan(comm, local, a.n_rolls, a.task_dist)
-    R = make_rank(local, rank, world, local_rank, a.dims, M, lb, tiling, plan, a.comm_type, a.platform, a.fetch_streams,
-                  fetch_scope=a.fetch_scope, pipeline=a.pipeline)
-    if comm is not None:
-        connect_peers(comm, R)
+
+    def new_rank():
+        X = make_rank(local, rank, world, local_rank, a.dims, M, lb, tiling, plan, a.comm_type, a.platform,
+                      a.fetch_streams, fetch_scope=a.fetch_scope, pipeline=a.pipeline)
+        if comm is not None:
+            connect_peers(comm, X)
+        return X
+
+    R = new_rank()
     st = R.stats()
     s = torch.cuda.Stream(dev)
     R.fill_b(a.seed + 1, s.cuda_stream)
     torch.cuda.synchronize(dev)
     if comm is not None:
         comm.barrier()
+    setup_s = time.perf_counter() - t_setup
     flush = torch.empty(512 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
 
     def flush_l2():
@@ -382,6 +513,18 @@ def main(argv=None):
     if clocks:
         clocks.mark(False)
     clk = clocks.stop() if clocks else None
+    R.check_error()
+
+    # the result of the timed steps, checked before anything else runs
+    if ub > lb:
+        torch.cuda.synchronize(dev)
+        Ch0 = np.empty((ub - lb, a.dims), np.float32)
+        R.download_c(Ch0)
+        torch.cuda.synchronize(dev)
+        n_dev, worst_dev = check_c(a, local, lambda r: Ch0[r], rank)
+        del Ch0
+    else:
+        n_dev, worst_dev = 0, 0.0
 
     # compute-stream time spent waiting for fetches in the last step (segments not back to back)
     segs = [(t[2], t[3]) for t in timeline if t[2] is not None]
@@ -401,94 +544,115 @@ def main(argv=None):
     peak, peak_kind = measured_peaks()
     achieved = alg_bytes / (mean_compute * 1e-3) / 1e9
 
-    # end to end through the C ABI: pinned host B (owned tiles uploaded), step, C to host
+    # end to end through the C ABI: pinned host B (the rank's owned tiles), step, C to host
     e2e = None
+    n_e2e_chk, worst_e2e = 0, 0.0
     if not a.no_e2e and not a.profile:
-        Bh = torch.empty((M, a.dims), dtype=torch.float32, pin_memory=True)
-        d.dense_b(M, a.dims, a.seed + 1, out=Bh.numpy())
-        # Steps back to back as an application runs them: B of step i+1 goes up (H2D
-        # stream) while C of step i comes down (D2H stream); each step waits for its B and
-        # for the previous C to have left the device, each upload for the previous step's
-        # reads of B. On one GPU a second rank object (when memory allows) double-buffers
-        # B and C, so the SpMM of step i+1 also overlaps the download of step i. Timed from
-        # the first upload to the last download of the K steps.
+        owned = R.owned_tiles()
+        n_owned = sum(n for _, n in owned)
+        Bh = torch.empty((max(n_owned, 1), a.dims), dtype=torch.float32, pin_memory=True)
+        o = 0
+        for row0, n in owned:
+            d.dense_b(n, a.dims, a.seed + 1, row0=row0, out=Bh.numpy()[o:o + n])
+            o += n
+        # Steps back to back as an application runs them, B and C double-buffered (a second
+        # rank object when memory allows): step i+1's upload (H2D stream) overlaps step i's
+        # SpMM and step i's download (D2H stream) overlaps step i+1's SpMM. Each upload waits
+        # until no rank reads that slot's B any more, each step until every rank's upload
+        # of its slot landed: with N > 1 both conditions are stream-ordered one-element NCCL
+        # all-reduces on a sync stream, so the host never blocks between steps.
         slots = [R]
-        if comm is None:
-            free, _ = torch.cuda.mem_get_info(dev)
-            if 4 * (M + (ub - lb)) * a.dims * 4 < free:
-                slots.append(make_rank(local, rank, world, local_rank, a.dims, M, lb, tiling, plan, a.comm_type,
-                                       a.platform, a.fetch_streams, fetch_scope=a.fetch_scope, pipeline=a.pipeline))
+        free, _ = torch.cuda.mem_get_info(dev)
+        room = 1.0 if st["device_bytes"] + (1 << 30) < free else 0.0
+        if comm is not None:  # the same choice on every rank (a second slot means collectives)
+            room = -comm.allreduce_max(-room)
+        if room > 0:
+            slots.append(new_rank())
         Chs = [torch.empty((max(ub - lb, 1), a.dims), dtype=torch.float32, pin_memory=True) for _ in slots]
-        s_up, s_dn = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        s_up, s_dn, s_sync = torch.cuda.Stream(dev), torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        tok = torch.zeros(1, dtype=torch.float32, device=dev)
+
+        def global_event(ev):
+            """An event that completes once `ev` completed on every rank."""
+            if comm is None:
+                return ev
+            s_sync.wait_event(ev)
+            with torch.cuda.stream(s_sync):
+                comm.dist.all_reduce(tok, group=comm.group)
+            g = torch.cuda.Event()
+            g.record(s_sync)
+            return g
 
         def e2e_run(n):
-            ev_comp, ev_dn = [None] * len(slots), [None] * len(slots)
-            last = None
+            ev_free, ev_dn = [None] * len(slots), [None] * len(slots)
             t0 = torch.cuda.Event(enable_timing=True)
             t1 = torch.cuda.Event(enable_timing=True)
             t0.record(s_up)
             for i in range(n):
                 k = i % len(slots)
                 X = slots[k]
-                if ev_comp[k] is not None:
-                    s_up.wait_event(ev_comp[k])  # X's B is free once its previous SpMM is done
-                if comm is not None and last is not None:  # ... on every rank: peers read its tiles
-                    last.synchronize()
-                    comm.barrier()
-                X.upload_b_ptr(Bh.data_ptr(), s_up.cuda_stream)
+                if ev_free[k] is not None:
+                    s_up.wait_event(ev_free[k])  # no rank reads X's B any more
+                X.upload_b_owned_ptr(Bh.data_ptr(), s_up.cuda_stream)
                 ev_up = torch.cuda.Event()
                 ev_up.record(s_up)
-                if comm is not None:  # peers read this rank's tiles only after every upload landed
-                    ev_up.synchronize()
-                    comm.barrier()
-                s.wait_event(ev_up)
+                s.wait_event(global_event(ev_up))  # every rank's owned tiles of this step landed
                 if ev_dn[k] is not None:
                     s.wait_event(ev_dn[k])  # X's C is free once its previous download is done
                 X.step(s.cuda_stream)
-                ev_comp[k] = last = torch.cuda.Event()
-                ev_comp[k].record(s)
-                s_dn.wait_event(ev_comp[k])
+                ev_comp = torch.cuda.Event()
+                ev_comp.record(s)
+                ev_free[k] = global_event(ev_comp)
+                s_dn.wait_event(ev_comp)
                 if ub > lb:
                     X.download_c_ptr(Chs[k].data_ptr(), s_dn.cuda_stream)
                 ev_dn[k] = torch.cuda.Event()
                 ev_dn[k].record(s_dn)
             t1.record(s_dn)
             t1.synchronize()
-            if comm is not None:
-                comm.barrier()
+            torch.cuda.synchronize(dev)
             return t0.elapsed_time(t1) / n
 
         e2e_run(max(a.warmup, 1))
         n_e2e = max(a.steps, 1)
         t_e2e = e2e_run(n_e2e)
         Ch = Chs[(n_e2e - 1) % len(slots)]
+        for X in slots:
+            X.check_error()
         for X in slots[1:]:
             X.close()
         if comm is not None:
+            comm.barrier()
             t_e2e = comm.allreduce_max(t_e2e)
-        # spot check of the result against the oracle on a few rows of this rank
-        import oracle
-        rng = np.random.default_rng(rank)
-        rows = rng.choice(ub - lb, size=min(64, ub - lb), replace=False) if ub > lb else np.zeros(0, int)
-        lens = np.diff(local.indptr)[rows]
-        ip = np.concatenate([[0], np.cumsum(lens)]).astype(np.int64)
-        sel = np.concatenate([np.arange(local.indptr[r], local.indptr[r + 1]) for r in rows]) if rows.size else \
-            np.zeros(0, np.int64)
-        ref, ab = oracle.spmm_f64(ip, local.indices[sel], local.values[sel], Bh.numpy())
-        ok, worst = oracle.check_close(Ch.numpy()[rows], ref, ab, 1e-5)
-        if comm is not None:
-            worst = comm.allreduce_max(worst)
-            ok = worst <= 1.0
+        if ub > lb:
+            n_e2e_chk, worst_e2e = check_c(a, local, lambda r: Ch.numpy()[r], rank)
         e2e = {"value": round(2.0 * nnz * a.dims / (t_e2e * 1e-3) / 1e9, 3), "unit": UNIT,
-               "ms_per_step": round(t_e2e, 4), "h2d_bytes_per_step": st["owned_rows"] * a.dims * 4,
+               "ms_per_step": round(t_e2e, 4), "h2d_bytes_per_step": n_owned * a.dims * 4,
                "d2h_bytes_per_step": (ub - lb) * a.dims * 4,
-               "overlap": "H2D of step i+1 with D2H of step i (pinned host buffers, separate streams)"
-                          + ("; B and C double-buffered (two rank objects), SpMM overlaps both" if len(slots) > 1 else ""),
-               "check": {"rows": int(rows.size), "worst_err_over_tol": round(worst, 4), "ok": bool(ok)}}
+               "overlap": "B and C double-buffered (two rank objects)" if len(slots) > 1 else "single buffer",
+               "sync": "stream-ordered one-element NCCL all-reduces" if comm is not None else "events"}
+        del Bh, Chs
+
+    # correctness of this rank's rows (device-timed steps and the e2e steps), all ranks
+    worst = max(worst_dev, worst_e2e)
+    n_chk = n_dev + n_e2e_chk
+    if comm is not None:
+        worst = comm.allreduce_max(worst)
+        n_chk = comm.allreduce_sum_i64(n_chk)
+    check = {"rows_checked_all_ranks": n_chk, "frac_per_rank": a.check_frac,
+             "plus_rows_longer_than": hub_degree(a), "worst_err_over_tol": round(worst, 4), "ok": bool(worst <= 1.0),
+             "tolerance": "|dC| <= 1e-5 * (|A|.|B|) elementwise vs the double-accumulated CPU oracle"}
 
     cpu = None
-    if rank == 0 and world == 1 and not a.no_cpu_baseline and not a.profile:
-        cpu = cpu_spmm_baseline(A, d.dense_b(M, a.dims, a.seed + 1))
+    cus = None
+    if world == 1 and not a.profile:
+        if not a.no_cusparse:
+            try:
+                cus = cusparse_arm(a, local, M, R, flush_l2, mean_compute)
+            except Exception as e:  # noqa: BLE001 — a comparison arm must not sink the line
+                cus = {"error": str(e)[:300]}
+        if not a.no_cpu_baseline:
+            cpu = cpu_spmm_baseline(local, a.dims, a.seed + 1)
 
     # Gather stream: every nonzero reads one B row of dims floats through L2 -> L1 (what
     # bounds a gather-per-nonzero kernel, next to the HBM roofline's algorithmic bytes).
@@ -506,32 +670,36 @@ def main(argv=None):
         per_rank = [[int(x) for x in r] for r in comm.allgather_i32(np.array(mine, np.int64).clip(max=2**31 - 1))]
     ranks = [{"nnz": r[0], "rows": r[1], "pipeline": ["", "rows", "split"][r[2]], "compute_ms": r[3] / 1e4,
               "idle_ms": r[4] / 1e4, "fetched_kib": r[5]} for r in per_rank]
+    traffic = profile_traffic(workload_name(a)) if world == 1 else None
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": a.steps,
         "warmup": a.warmup, "ms_per_step": round(t_step, 4), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config_of(a, world, nnz, M),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "traffic": profile_traffic(workload_name(a)),
+                     "frac": round(achieved / peak, 4), "traffic": traffic,
                      "kernel": "spmm_nnz_kernel / spmm_rows_kernel (+fixup, zero rows)", "rank": rank,
                      "alg_bytes_per_launch": alg_bytes, "launch_ms": round(mean_compute, 4),
                      "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})"},
-        "e2e": e2e, "cpu_baseline": cpu, "clocks": clk,
+        "e2e": e2e, "cpu_baseline": cpu, "cusparse": cus, "check": check, "clocks": clk,
         "gpu_launches": a.steps * st["kernels_per_step"],
         "nvlink": {"fetched_bytes_per_step": fetch_bytes, "pipeline_rank0": ["", "rows", "split"][st["pipeline"]],
                    "phase0_nnz_rank0": st["phase0_nnz"],
                    "max_rank_compute_ms": round(t_comp_max, 4),
                    "max_rank_compute_idle_ms": round(idle_max, 4),
                    "timeline_rank0": timeline if rank == 0 else None, "ranks": ranks},
-        "wall_s_timed_region": round(wall, 3),
+        "wall_s_timed_region": round(wall, 3), "setup_s": round(setup_s, 1),
         "gather": gather,
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
     R.close()
     if comm is not None:
+        comm.barrier()
+        if cleanup:
+            cleanup()
         import torch.distributed as dist
         dist.destroy_process_group()
-    return 0
+    return 0 if check["ok"] else 1
 
 
 if __name__ == "__main__":

@@ -343,6 +343,121 @@ __global__ void __launch_bounds__(kSpmmThreads) spmm_nnz_kernel(const SpmmArgs a
   if (!kAccum && chunk == a.n_chunks - 1) zero_rows<LPR, VPL, W>(a, (int64_t)row + 1, a.zero_rows, col0);
 }
 
+// ------------------------------------------------------------------ nnz-split, warp per chunk
+
+// (column, value) pairs of 4 consecutive nonzeros, read by every lane of the warp from the
+// same 16-byte address (one L1 wavefront each, served to all lanes).
+__device__ __forceinline__ int4 ldg_uniform_i4(const int32_t *p) {
+  int4 v;
+  asm("ld.global.nc.L1::evict_last.v4.s32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ float4 ldg_uniform_f4(const float *p) {
+  float4 v;
+  asm("ld.global.nc.L1::evict_last.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
+  return v;
+}
+
+// One chunk of chunk_nnz consecutive nonzeros per warp; lane l holds output columns
+// col0 + 128 v .. +3 (v < VPL) of the current row, blockIdx.y selecting a block of
+// 128 * VPL columns. Each step reads the (column, value) pairs of U nonzeros with uniform
+// vector loads, issues their U B-row loads (one 512-byte row per warp instruction at
+// VPL = 1, all U in flight together), then does the FMAs. Rows are the operand's listed
+// rows: a row change is met when the nonzero position reaches the current row's end
+// (lrow_ptr), which is the same for every lane, so no per-nonzero row ids are read and
+// no lane diverges. Listed rows without nonzeros that a chunk walks past are written as
+// zeros (non-accumulating launches); cut rows go to their partial slots as in
+// spmm_nnz_kernel. Needs N % (128 * VPL) == 0, 16-byte aligned B / C rows, chunk_nnz a
+// multiple of kWarpChunkAlign and cols / vals padded by kWarpChunkPad entries.
+template <int VPL, int U, bool kAccum>
+__global__ void __launch_bounds__(kSpmmThreads) spmm_warp_kernel(const SpmmArgs a) {
+  static_assert(U % 4 == 0 && U <= kWarpChunkPad && kWarpChunkAlign % U == 0, "U");
+  using V = Vec<4>;
+  const int lane = threadIdx.x & 31;
+  const int64_t chunk = ((int64_t)blockIdx.x * kSpmmThreads + threadIdx.x) >> 5;
+  if (chunk >= a.n_chunks) return;
+  const int col0 = blockIdx.y * (128 * VPL) + lane * 4;
+  const int64_t s = chunk * a.chunk_nnz, e = min(s + a.chunk_nnz, a.nnz);
+  const int32_t head_slot = a.chunk_slot[2 * chunk], tail_slot = a.chunk_slot[2 * chunk + 1];
+  const uint64_t pol = evict_last_policy();
+
+  int64_t lr = a.chunk_lrow[chunk];
+  const int64_t head_lr = lr;
+  // the chunk's first row is its head slot's only when that row began in an earlier chunk
+  // (otherwise chunk_lrow may name empty rows before the first row holding a nonzero, and a
+  // single cut row's slot is the tail slot)
+  const int32_t head = __ldg(a.lrow_ptr + lr) < s ? head_slot : -1;
+  int64_t rend = __ldg(a.lrow_ptr + lr + 1);
+  bool touched = false;  // the current row received a nonzero of this chunk
+  float4 acc[VPL];
+#pragma unroll
+  for (int w = 0; w < VPL; ++w) acc[w] = V::zero();
+
+  // Write listed row lr (to its slot, or C); an accumulating launch skips rows that got no
+  // nonzero here, a writing one writes them (their zeros).
+  auto flush = [&](int32_t slot) {
+    const int32_t row = a.lrow_out ? __ldg(a.lrow_out + lr) : (int32_t)lr;
+    if (slot >= 0) {
+      float *dst = a.partial + (int64_t)slot * a.N + col0;
+#pragma unroll
+      for (int w = 0; w < VPL; ++w) V::st(dst + 128 * w, acc[w]);
+    } else if (!(accumulates<kAccum>(a, row) && !touched)) {
+      float *dst = a.C + (int64_t)row * a.ldc + col0;
+      const bool add = accumulates<kAccum>(a, row);
+#pragma unroll
+      for (int w = 0; w < VPL; ++w) {
+        float4 r = acc[w];
+        if (add) V::add(r, V::ld(dst + 128 * w));
+        V::st_stream(dst + 128 * w, r);
+      }
+    }
+  };
+
+  for (int64_t base = s; base < e; base += U) {
+    int c[U];
+    float v[U];
+#pragma unroll
+    for (int q = 0; q < U / 4; ++q) {
+      const int4 c4 = ldg_uniform_i4(a.cols + base + 4 * q);
+      const float4 v4 = ldg_uniform_f4(a.vals + base + 4 * q);
+      c[4 * q] = c4.x, c[4 * q + 1] = c4.y, c[4 * q + 2] = c4.z, c[4 * q + 3] = c4.w;
+      v[4 * q] = v4.x, v[4 * q + 1] = v4.y, v[4 * q + 2] = v4.z, v[4 * q + 3] = v4.w;
+    }
+    float4 b[U][VPL];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const float *brow = a.B + (int64_t)c[u] * a.ldb + col0;
+#pragma unroll
+      for (int w = 0; w < VPL; ++w) b[u][w] = base + u < e ? V::ldg(brow + 128 * w, pol) : V::zero();
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t p = base + u;
+      if (p < e) {
+        while (p >= rend) {  // warp-uniform: the chunk moves on to a later listed row
+          flush(lr == head_lr ? head : -1);
+          ++lr;
+          rend = __ldg(a.lrow_ptr + lr + 1);
+          touched = false;
+#pragma unroll
+          for (int w = 0; w < VPL; ++w) acc[w] = V::zero();
+        }
+#pragma unroll
+        for (int w = 0; w < VPL; ++w) V::fma(acc[w], v[u], b[u][w]);
+        touched = true;
+      }
+    }
+  }
+  flush(tail_slot >= 0 ? tail_slot : (lr == head_lr ? head : -1));
+  // the last chunk writes the listed rows after its last nonzero (all empty)
+  if (!kAccum && a.zero_rows > 0 && chunk == a.n_chunks - 1) {
+    touched = false;
+#pragma unroll
+    for (int w = 0; w < VPL; ++w) acc[w] = V::zero();
+    for (++lr; lr < a.n_lrows; ++lr) flush(-1);
+  }
+}
+
 // ------------------------------------------------------------------ fixup and fills
 
 // One warp per cut row: C[row] = (accumulating ? C[row] : 0) + sum of its partial slots,
@@ -450,6 +565,51 @@ KernelFn select_kernel(int variant, int W, bool accum, int LPR, int VPL) {
 
 bool aligned(const void *p, uintptr_t bytes) { return ((uintptr_t)p & (bytes - 1)) == 0; }
 
+// Warp-per-chunk shapes (vectors of 4 floats per lane per 128 columns, nonzeros per step).
+#define DSP_WARP_SHAPES(X) X(1, 4) X(1, 8) X(1, 16) X(2, 4) X(2, 8) X(4, 4)
+
+KernelFn warp_kernel_for(int VPL, int U, bool accum) {
+#define DSP_WK(P, Q) \
+  if (VPL == P && U == Q) return accum ? spmm_warp_kernel<P, Q, true> : spmm_warp_kernel<P, Q, false>;
+  DSP_WARP_SHAPES(DSP_WK)
+#undef DSP_WK
+  return nullptr;
+}
+
+// The warp-per-chunk kernel's shape for a launch, or VPL = 0 when it does not apply (the
+// lane-group kernels then run): N a multiple of 128, 16-byte aligned rows of B and C.
+// DSP_SPMM_WARP=0 turns it off; DSP_SPMM_WARP_VPL / DSP_SPMM_WARP_U force a shape (sweeps).
+struct WarpShape {
+  int VPL = 0, U = 0, gy = 0;
+};
+WarpShape warp_shape(int N, const float *B, int64_t ldb, const float *C, int64_t ldc) {
+  static const int env_on = [] {
+    const char *e = getenv("DSP_SPMM_WARP");
+    return e ? atoi(e) : 1;
+  }();
+  static const int env_vpl = [] {
+    const char *e = getenv("DSP_SPMM_WARP_VPL");
+    return e ? atoi(e) : 0;
+  }();
+  static const int env_u = [] {
+    const char *e = getenv("DSP_SPMM_WARP_U");
+    return e ? atoi(e) : 0;
+  }();
+  WarpShape w;
+  if (!env_on || N <= 0 || N % 128 != 0 || ldb % 4 != 0 || ldc % 4 != 0 || !aligned(B, 16) || !aligned(C, 16))
+    return w;
+  const int n128 = N / 128;
+  int vpl = n128 % 4 == 0 ? 4 : n128 % 2 == 0 ? 2 : 1;
+  if (env_vpl > 0 && n128 % env_vpl == 0) vpl = env_vpl;
+  int u = vpl == 1 ? 8 : 4;
+  if (env_u > 0) u = env_u;
+  if (!warp_kernel_for(vpl, u, false)) return w;
+  w.VPL = vpl;
+  w.U = u;
+  w.gy = n128 / vpl;
+  return w;
+}
+
 }  // namespace
 
 SpmmShape spmm_shape(int N, int variant, const float *B, int64_t ldb, const float *C, int64_t ldc, int max_w) {
@@ -517,7 +677,15 @@ int launch_spmm(const SpmmArgs &a, bool accumulate, cudaStream_t stream) {
   const SpmmShape s = spmm_shape(a.N, a.variant, a.B, a.ldb, a.C, a.ldc);
   if (s.chunks > 65535) return fail(DSP_ERR_UNSUPPORTED, "spmm: N = %d too wide", a.N);
   const int64_t units = a.variant == kRowSplit ? a.n_items : a.n_chunks;
-  if (units > 0) {
+  const WarpShape ws = a.variant == kNnzSplit && a.lrow_ptr && a.chunk_lrow && a.chunk_nnz % kWarpChunkAlign == 0
+                           ? warp_shape(a.N, a.B, a.ldb, a.C, a.ldc)
+                           : WarpShape();
+  if (units > 0 && ws.VPL > 0) {
+    KernelFn k = warp_kernel_for(ws.VPL, ws.U, accumulate);
+    const int64_t gx = (units + kSpmmThreads / 32 - 1) / (kSpmmThreads / 32);
+    if (gx > INT32_MAX) return fail(DSP_ERR_UNSUPPORTED, "spmm: %lld work units", (long long)units);
+    k<<<dim3((unsigned)gx, (unsigned)ws.gy), kSpmmThreads, 0, stream>>>(a);
+  } else if (units > 0) {
     KernelFn k = select_kernel(a.variant, s.W, accumulate, s.LPR, s.VPL);
     const int64_t groups_per_block = kSpmmThreads / s.LPR;
     const int64_t gx = (units + groups_per_block - 1) / groups_per_block;
@@ -579,7 +747,9 @@ int64_t wave_chunk_nnz(int device, int dims, int64_t nnz) {
   const float *aligned_ptr = reinterpret_cast<const float *>(uintptr_t(256));
   const int ld = (dims + 7) & ~7;
   const SpmmShape sh = spmm_shape(dims, kNnzSplit, aligned_ptr, ld, aligned_ptr, ld);
-  KernelFn k = select_kernel(kNnzSplit, sh.W, false, sh.LPR, sh.VPL);
+  const WarpShape ws = warp_shape(dims, aligned_ptr, ld, aligned_ptr, ld);
+  KernelFn k = ws.VPL > 0 ? warp_kernel_for(ws.VPL, ws.U, false) : select_kernel(kNnzSplit, sh.W, false, sh.LPR, sh.VPL);
+  const int lanes = ws.VPL > 0 ? 32 : sh.LPR, col_blocks = ws.VPL > 0 ? ws.gy : sh.chunks;
   int sms = 0, per_sm = 0;
   if (!k || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess ||
       cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kSpmmThreads, 0) != cudaSuccess || sms <= 0 ||
@@ -587,9 +757,10 @@ int64_t wave_chunk_nnz(int device, int dims, int64_t nnz) {
     cudaGetLastError();
     return c;
   }
-  const int64_t resident = (int64_t)sms * per_sm * (kSpmmThreads / sh.LPR) / std::max(sh.chunks, 1);
+  const int64_t resident = (int64_t)sms * per_sm * (kSpmmThreads / lanes) / std::max(col_blocks, 1);
   const int64_t waves = std::max<int64_t>(2, (nnz + c * resident - 1) / (c * resident));
-  return std::max<int64_t>(8, (nnz + waves * resident - 1) / (waves * resident));
+  const int64_t len = std::max<int64_t>(8, (nnz + waves * resident - 1) / (waves * resident));
+  return (len + kWarpChunkAlign - 1) / kWarpChunkAlign * kWarpChunkAlign;
 }
 
 int DevOperand::upload(int device_, int64_t rows_, int64_t cols_, const int64_t *row_ptr, const int32_t *row_ids,
@@ -628,34 +799,49 @@ int DevOperand::upload(int device_, int64_t rows_, int64_t cols_, const int64_t 
     max_row_len = plan.max_row_len;
     split_row.swap(plan.split_row);
     split_ptr.swap(plan.split_ptr);
+    n_lrows = m;
     if ((rc = dev_upload(&d_coo_row, plan.coo_row.data(), sizeof(int32_t) * (size_t)nnz)) ||
-        (rc = dev_upload(&d_chunk_slot, plan.chunk_slot.data(), sizeof(int32_t) * (size_t)(2 * n_chunks))))
+        (rc = dev_upload(&d_chunk_slot, plan.chunk_slot.data(), sizeof(int32_t) * (size_t)(2 * n_chunks))) ||
+        (rc = dev_upload(&d_chunk_lrow, plan.chunk_lrow.data(), sizeof(int32_t) * (size_t)n_chunks)) ||
+        (rc = dev_upload(&d_lrow_ptr, rp.data(), sizeof(int64_t) * (size_t)(m + 1))) ||
+        (row_ids && (rc = dev_upload(&d_lrow_out, row_ids, sizeof(int32_t) * (size_t)m))))
       return rc;
   }
   n_split = (int64_t)split_row.size();
-  std::vector<int32_t> c32((size_t)std::max<int64_t>(nnz, 1));
+  // column ids (int32) and values, padded with kWarpChunkPad zero entries for the vector
+  // reads of the warp-per-chunk kernel
+  const int64_t padded = nnz + kWarpChunkPad;
+  std::vector<int32_t> c32((size_t)padded, 0);
+  std::vector<float> v32((size_t)padded, 0.f);
   parallel_for(nnz, [&](int64_t b, int64_t e) {
-    for (int64_t j = b; j < e; ++j) c32[(size_t)j] = (int32_t)indices[first_nz + j];
+    for (int64_t j = b; j < e; ++j) {
+      c32[(size_t)j] = (int32_t)indices[first_nz + j];
+      v32[(size_t)j] = values[first_nz + j];
+    }
   }, 1 << 16);
   if ((rc = dev_upload(&d_split_row, split_row.data(), sizeof(int32_t) * split_row.size())) ||
       (rc = dev_upload(&d_split_ptr, split_ptr.data(), sizeof(int32_t) * split_ptr.size())) ||
-      (rc = dev_upload(&d_cols, c32.data(), sizeof(int32_t) * (size_t)nnz)) ||
-      (rc = dev_upload(&d_vals, values + first_nz, sizeof(float) * (size_t)nnz)))
+      (rc = dev_upload(&d_cols, c32.data(), sizeof(int32_t) * (size_t)padded)) ||
+      (rc = dev_upload(&d_vals, v32.data(), sizeof(float) * (size_t)padded)))
     return rc;
   return DSP_OK;
 }
 
 void DevOperand::release() {
   for (void **p : {(void **)&d_item_ptr, (void **)&d_item_out, (void **)&d_coo_row, (void **)&d_chunk_slot,
-                   (void **)&d_split_row, (void **)&d_split_ptr, (void **)&d_cols, (void **)&d_vals}) {
+                   (void **)&d_chunk_lrow, (void **)&d_lrow_ptr, (void **)&d_lrow_out, (void **)&d_split_row,
+                   (void **)&d_split_ptr, (void **)&d_cols, (void **)&d_vals}) {
     if (*p) cudaFree(*p);
     *p = nullptr;
   }
-  n_items = n_chunks = n_split = pieces = 0;
+  n_items = n_chunks = n_split = pieces = n_lrows = 0;
 }
 
 int64_t DevOperand::device_bytes() const {
-  return n_items * 12 + 8 + n_chunks * 8 + (variant == kNnzSplit ? nnz * 4 : 0) + n_split * 8 + 4 + nnz * 8;
+  const int64_t nnz_split = variant == kNnzSplit
+                                ? nnz * 4 + n_chunks * 4 + (n_lrows + 1) * 8 + (d_lrow_out ? n_lrows * 4 : 0)
+                                : 0;
+  return n_items * 12 + 8 + n_chunks * 8 + nnz_split + n_split * 8 + 4 + (nnz + kWarpChunkPad) * 8;
 }
 
 SpmmArgs DevOperand::args(const float *B, int64_t ldb, float *C, int64_t ldc, int N, float *partial) const {
@@ -667,6 +853,10 @@ SpmmArgs DevOperand::args(const float *B, int64_t ldb, float *C, int64_t ldc, in
   a.n_items = n_items;
   a.coo_row = d_coo_row;
   a.chunk_slot = d_chunk_slot;
+  a.lrow_ptr = d_lrow_ptr;
+  a.lrow_out = d_lrow_out;
+  a.chunk_lrow = d_chunk_lrow;
+  a.n_lrows = n_lrows;
   a.n_chunks = n_chunks;
   a.chunk_nnz = chunk_nnz;
   a.nnz = nnz;
@@ -709,6 +899,12 @@ void prefer_l1_carveout() {
             if (shape_supported(w, lpr, vpl))
               cudaFuncSetAttribute(select_kernel(v, w, acc != 0, lpr, vpl),
                                    cudaFuncAttributePreferredSharedMemoryCarveout, 0);
+  for (int acc = 0; acc < 2; ++acc) {
+#define DSP_WC(P, Q) \
+  cudaFuncSetAttribute(warp_kernel_for(P, Q, acc != 0), cudaFuncAttributePreferredSharedMemoryCarveout, 0);
+    DSP_WARP_SHAPES(DSP_WC)
+#undef DSP_WC
+  }
   cudaGetLastError();
   if (dev < 31) done_mask |= 1 << dev;
 }

@@ -12,9 +12,13 @@ What it holds
   * ``libdsp_ref.so`` (ref_shim.cpp, optional): the reference's own ``src/h_sdma.h`` and
     ``src/sparse_matrix.h`` compiled from the reference sources, used to pin the
     restatement (HSDMA, loader) and to generate the golden fixtures.
+  * ``libdsp_ref_mpi.so`` (ref_mpi_shim.cu, optional): the reference's MPI-bound
+    ``src/utils.h`` (node merge, HSDMA MPI wrapper) compiled against the thread-rank MPI
+    stand-in of ``mpi_stub/`` and run with one thread per rank.
 
-Parity: HSDMA and the loader are pinned to the reference build; tiling / merge /
-selector / traffic restate MPI-bound code that cannot be built here; SpMM values are
+Parity: HSDMA, its MPI wrapper, the node merge and the loader are pinned to the reference
+build; tiling (inside the reference's main()), selector and traffic restate code that
+cannot be built here; SpMM values are
 "parity unpinned" against the reference (it never checks C) and use the elementwise
 bound max|dC| <= 1e-5 * (|A|.|B|).
 """
@@ -29,6 +33,7 @@ import numpy as np
 _HERE = os.path.dirname(os.path.abspath(__file__))
 _LIB = os.path.join(_HERE, "_build", "liboracle.so")
 _REF = os.path.join(_HERE, "_ref", "libdsp_ref.so")
+_REF_MPI = os.path.join(_HERE, "_ref", "libdsp_ref_mpi.so")
 
 _i64p = ctypes.POINTER(ctypes.c_int64)
 _i32p = ctypes.POINTER(ctypes.c_int32)
@@ -38,6 +43,7 @@ _f64p = ctypes.POINTER(ctypes.c_double)
 
 _lib = None
 _ref = None
+_ref_mpi = None
 
 
 def build(ref: bool = True, ref_src: str | None = None) -> None:
@@ -95,6 +101,50 @@ def ref_lib():
                                    _i64p, _i64p, _i64p, _f32p]
         _ref = R
     return _ref
+
+
+def ref_mpi_lib():
+    """The reference's MPI-bound utils.h behind ref_mpi_shim.cu, or None if not built here."""
+    global _ref_mpi
+    if _ref_mpi is None and os.path.exists(_REF_MPI):
+        R = ctypes.CDLL(_REF_MPI)
+        R.ref_node_merge.argtypes = [ctypes.c_int, ctypes.c_int, _i32p, _i32p, _i32p, _i64p, _i32p]
+        R.ref_hsdma_mpi.argtypes = [ctypes.c_int, ctypes.c_int, _i32p, _i32p, ctypes.c_int, _i32p]
+        _ref_mpi = R
+    return _ref_mpi
+
+
+def ref_node_merge(counts, cols):
+    """double_level_comm_node_processing (src/utils.h:439-547) of the reference, on one
+    thread per rank. counts: R x T pre-merge sizes; cols: flat rank-major, tile-major lists.
+    Returns (merged counts, offsets, merged lists ascending) like merge()."""
+    R = ref_mpi_lib()
+    if R is None:
+        raise RuntimeError("reference MPI shim not built")
+    counts = np.ascontiguousarray(counts, np.int32)
+    cols = np.ascontiguousarray(cols, np.int32) if np.size(cols) else np.zeros(1, np.int32)
+    P, T = counts.shape
+    n = np.zeros(T, np.int32)
+    off = np.zeros(T + 1, np.int64)
+    if R.ref_node_merge(P, T, _p(counts, _i32p), _p(cols, _i32p), _p(n, _i32p), _p(off, _i64p), None) != 0:
+        raise RuntimeError("ranks disagree after the reference merge")
+    out = np.zeros(max(int(off[-1]), 1), np.int32)
+    R.ref_node_merge(P, T, _p(counts, _i32p), _p(cols, _i32p), _p(n, _i32p), _p(off, _i64p), _p(out, _i32p))
+    return n, off, out[: int(off[-1])]
+
+
+def ref_hsdma_mpi(demand, node_of_gpu, tasks_per_gpu):
+    """ComputeAllocation_HSDMA_MPI (src/utils.h:358-437) of the reference, on one thread per
+    rank, each with its own demand row. Returns the P x T remap every rank holds."""
+    R = ref_mpi_lib()
+    if R is None:
+        raise RuntimeError("reference MPI shim not built")
+    demand = np.ascontiguousarray(demand, np.int32)
+    P, T = demand.shape
+    nodes = np.ascontiguousarray(node_of_gpu, np.int32)
+    remap = np.zeros(P * T, np.int32)
+    R.ref_hsdma_mpi(P, T, _p(demand, _i32p), _p(nodes, _i32p), tasks_per_gpu, _p(remap, _i32p))
+    return remap.reshape(P, T)
 
 
 # ---------------------------------------------------------------- SpMM

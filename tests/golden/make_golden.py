@@ -14,6 +14,14 @@ Fixtures and their source of truth:
                        src/comm_man.h:396-400 evaluated by an nvcc-compiled probe
                        (oracle/threshold_probe.cu), bit patterns, for the H100 and A800
                        constants and dims 1..2048.
+  merge_cases.json     the node union of the ranks' needed sets from the reference's own
+                       double_level_comm_node_processing (src/utils.h:439-547), compiled
+                       with the thread-rank MPI stand-in (oracle/_ref/libdsp_ref_mpi.so) and
+                       run with one thread per rank: inputs (per-rank counts and lists of
+                       small R-MAT / stencil / uniform tilings) and the merged counts and
+                       ascending lists.
+  hsdma_mpi_cases.json remap[] every rank holds after the reference's ComputeAllocation_
+                       HSDMA_MPI (src/utils.h:358-437), same build, seeded random demands.
   comm_model_fit.json  the reference's own model fit (tools/fit_comm_model.py, imported
                        from the reference tree): the (dims, mean critical density) inputs
                        it fits per tier and the (a, b, c, u) it returns.
@@ -54,6 +62,44 @@ def make_hsdma():
         cases.append(dict(demand=D.tolist(), node_of_gpu=node.tolist(), tasks_per_gpu=rolls,
                           max_inter=it[0], max_intra=it[1], remap=remap.tolist()))
     with open(os.path.join(HERE, "hsdma_cases.json"), "w") as f:
+        json.dump(cases, f)
+
+
+def make_merge():
+    import distspmm_b200 as d
+    from distspmm_b200 import planner
+    cases = []
+    mats = [("rmat10", d.gen_rmat(10, seed=11)), ("stencil6", d.gen_stencil27(6, seed=12)),
+            ("uniform600x5", d.gen_uniform(600, 5, seed=13))]
+    for name, A in mats:
+        for P, rolls in ((2, 4), (3, 2), (4, 1), (8, 4)):
+            T = P * rolls
+            tilings = [planner.tile(planner.partition(A, *planner.bounds(A, P, p, "rows")), T) for p in range(P)]
+            counts = np.stack([t.n_col for t in tilings]).astype(np.int32)
+            flat = np.concatenate([t.needed for t in tilings]).astype(np.int32)
+            n, off, merged = oracle.ref_node_merge(counts, flat)
+            cases.append(dict(matrix=name, P=P, n_rolls=rolls, cpt=int(tilings[0].cpt), counts=counts.tolist(),
+                              lists=flat.tolist(), merged_count=n.tolist(), offsets=off.tolist(),
+                              merged=merged.tolist()))
+    with open(os.path.join(HERE, "merge_cases.json"), "w") as f:
+        json.dump(cases, f)
+
+
+def make_hsdma_mpi():
+    rng = np.random.default_rng(20240602)
+    cases = []
+    for _ in range(24):
+        P = int(rng.choice([1, 2, 3, 4, 8]))
+        nodes = int(rng.choice([n for n in (1, 2, 4) if P % n == 0]))
+        rolls = int(rng.integers(1, 5))
+        T = P * rolls
+        D = rng.integers(0, int(rng.choice([3, 60, 50000])), size=(P, T)).astype(np.int32)
+        node = np.repeat(np.arange(nodes), P // nodes).astype(np.int32)
+        remap = oracle.ref_hsdma_mpi(D, node, rolls)
+        assert (remap == remap[0]).all()
+        cases.append(dict(demand=D.tolist(), node_of_gpu=node.tolist(), tasks_per_gpu=rolls,
+                          remap=remap[0].tolist()))
+    with open(os.path.join(HERE, "hsdma_mpi_cases.json"), "w") as f:
         json.dump(cases, f)
 
 
@@ -110,9 +156,11 @@ def make_fit(ref_root=None):
 if __name__ == "__main__":
     make_fit()
     oracle.build(ref=True, ref_src=os.path.join(os.environ["DSP_REFERENCE_ROOT"], "src"))
-    if oracle.ref_lib() is None:
+    if oracle.ref_lib() is None or oracle.ref_mpi_lib() is None:
         sys.exit("reference shim not available: run where the reference sources exist")
     make_hsdma()
+    make_merge()
+    make_hsdma_mpi()
     make_csr()
     make_thresholds()
     print("golden fixtures written to", HERE)

@@ -183,3 +183,41 @@ def test_fetch_view_scopes(rmat):
         assert own <= union
     with pytest.raises(ValueError):
         fetch_view(plan, tilings[1], "cluster")
+
+
+def test_merge_matches_reference_merge_golden():
+    """Node union of the ranks' needed sets: the engine's dsp_merge_needed and the oracle
+    restatement against the reference's own double_level_comm_node_processing
+    (src/utils.h:439-547), run with one thread per rank (tests/golden/merge_cases.json)."""
+    for c in json.load(open(os.path.join(GOLDEN, "merge_cases.json"))):
+        counts = np.array(c["counts"], np.int32)
+        flat = np.array(c["lists"], np.int32)
+        n, off, merged = planner.merge_needed(counts, flat)
+        assert n.tolist() == c["merged_count"], (c["matrix"], c["P"])
+        assert off.tolist() == c["offsets"] and merged.tolist() == c["merged"]
+        n2, off2, m2 = oracle.merge(counts, flat, c["cpt"])
+        assert n2.tolist() == c["merged_count"] and m2.tolist() == c["merged"]
+
+
+def test_hsdma_mpi_wrapper_matches_reference_golden():
+    """The distributed allocation (every rank computes HSDMA from the all-gathered demand)
+    gives the remap that every rank holds after the reference's ComputeAllocation_HSDMA_MPI
+    (Gather to the root, HSDMA there, Bcast; src/utils.h:358-437)."""
+    for c in json.load(open(os.path.join(GOLDEN, "hsdma_mpi_cases.json"))):
+        D = np.array(c["demand"], np.int32)
+        got = planner.hierarchical_iterative_refinement_allocation(D, np.array(c["node_of_gpu"], np.int32),
+                                                                   c["tasks_per_gpu"])
+        assert got.tolist() == c["remap"]
+
+
+@pytest.mark.skipif(oracle.ref_mpi_lib() is None, reason="reference MPI shim not built here")
+def test_merge_random_vs_reference_build(rmat):
+    """Live check against the reference's merge on tilings of a fresh matrix."""
+    for P, rolls in ((2, 3), (5, 2)):
+        T = P * rolls
+        tilings = [planner.tile(planner.partition(rmat, *planner.bounds(rmat, P, p, "rows")), T) for p in range(P)]
+        counts = np.stack([t.n_col for t in tilings])
+        flat = np.concatenate([t.needed for t in tilings])
+        want = oracle.ref_node_merge(counts, flat)
+        got = planner.merge_needed(counts, flat)
+        assert all(np.array_equal(a, b) for a, b in zip(got, want))
