@@ -27,6 +27,7 @@
 #include <string.h>
 
 #include <mutex>
+#include <type_traits>
 
 #include "device.cuh"
 #include "internal.h"
@@ -360,18 +361,20 @@ __device__ __forceinline__ float4 ldg_uniform_f4(const float *p) {
 
 // One chunk of chunk_nnz consecutive nonzeros per warp; lane l holds output columns
 // col0 + 128 v .. +3 (v < VPL) of the current row, blockIdx.y selecting a block of
-// 128 * VPL columns. Each step reads the (column, value) pairs of U nonzeros with uniform
-// vector loads, issues their U B-row loads (one 512-byte row per warp instruction at
-// VPL = 1, all U in flight together), then does the FMAs. Rows are the operand's listed
-// rows: a row change is met when the nonzero position reaches the current row's end
-// (lrow_ptr), which is the same for every lane, so no per-nonzero row ids are read and
-// no lane diverges. Listed rows without nonzeros that a chunk walks past are written as
-// zeros (non-accumulating launches); cut rows go to their partial slots as in
-// spmm_nnz_kernel. Needs N % (128 * VPL) == 0, 16-byte aligned B / C rows, chunk_nnz a
-// multiple of kWarpChunkAlign and cols / vals padded by kWarpChunkPad entries.
+// 128 * VPL columns. The chunk is walked U nonzeros per step, software-pipelined: the
+// (column, value) pairs of step i + 2 are read (uniform vector loads) and the U B rows of
+// step i + 1 are requested (one 512-byte row per warp instruction at VPL = 1) before the
+// FMAs of step i, so 2U row loads are in flight behind the arithmetic. Rows are the
+// operand's listed rows; the boundaries and output rows of 32 consecutive listed rows sit
+// one per lane (read once per 32 rows), so a row change costs two shuffles and no memory
+// wait, and is the same for every lane (no divergence). Listed rows without nonzeros that
+// a chunk walks past are written as zeros (non-accumulating launches); cut rows go to
+// their partial slots as in spmm_nnz_kernel. Needs N % (128 * VPL) == 0, 16-byte aligned
+// B / C rows, chunk_nnz a multiple of kWarpChunkAlign and cols / vals padded by
+// kWarpChunkPad entries.
 template <int VPL, int U, bool kAccum>
 __global__ void __launch_bounds__(kSpmmThreads) spmm_warp_kernel(const SpmmArgs a) {
-  static_assert(U % 4 == 0 && U <= kWarpChunkPad && kWarpChunkAlign % U == 0, "U");
+  static_assert(U % 4 == 0 && 2 * U <= kWarpChunkPad && kWarpChunkAlign % U == 0, "U");
   using V = Vec<4>;
   const int lane = threadIdx.x & 31;
   const int64_t chunk = ((int64_t)blockIdx.x * kSpmmThreads + threadIdx.x) >> 5;
@@ -381,80 +384,126 @@ __global__ void __launch_bounds__(kSpmmThreads) spmm_warp_kernel(const SpmmArgs 
   const int32_t head_slot = a.chunk_slot[2 * chunk], tail_slot = a.chunk_slot[2 * chunk + 1];
   const uint64_t pol = evict_last_policy();
 
+  // window of listed rows [w0, w0 + 32): lane j holds the end of row w0 + j and its output row
   int64_t lr = a.chunk_lrow[chunk];
   const int64_t head_lr = lr;
+  int64_t w0 = lr;
+  int64_t w_end = 0;
+  int32_t w_out = 0;
+  auto load_window = [&]() {
+    const int64_t r = w0 + lane;
+    w_end = r < a.n_lrows ? __ldg(a.lrow_ptr + r + 1) : INT64_MAX;
+    w_out = r < a.n_lrows ? (a.lrow_out ? __ldg(a.lrow_out + r) : (int32_t)r) : 0;
+  };
+  load_window();
+  int64_t rend = __shfl_sync(0xffffffffu, w_end, 0);
+  int32_t row = __shfl_sync(0xffffffffu, w_out, 0);
   // the chunk's first row is its head slot's only when that row began in an earlier chunk
   // (otherwise chunk_lrow may name empty rows before the first row holding a nonzero, and a
   // single cut row's slot is the tail slot)
   const int32_t head = __ldg(a.lrow_ptr + lr) < s ? head_slot : -1;
-  int64_t rend = __ldg(a.lrow_ptr + lr + 1);
   bool touched = false;  // the current row received a nonzero of this chunk
   float4 acc[VPL];
 #pragma unroll
   for (int w = 0; w < VPL; ++w) acc[w] = V::zero();
 
-  // Write listed row lr (to its slot, or C); an accumulating launch skips rows that got no
+  // Write the current row (to its slot, or C); an accumulating launch skips rows that got no
   // nonzero here, a writing one writes them (their zeros).
   auto flush = [&](int32_t slot) {
-    const int32_t row = a.lrow_out ? __ldg(a.lrow_out + lr) : (int32_t)lr;
     if (slot >= 0) {
       float *dst = a.partial + (int64_t)slot * a.N + col0;
 #pragma unroll
       for (int w = 0; w < VPL; ++w) V::st(dst + 128 * w, acc[w]);
-    } else if (!(accumulates<kAccum>(a, row) && !touched)) {
-      float *dst = a.C + (int64_t)row * a.ldc + col0;
+    } else {
       const bool add = accumulates<kAccum>(a, row);
+      if (!(add && !touched)) {
+        float *dst = a.C + (int64_t)row * a.ldc + col0;
 #pragma unroll
-      for (int w = 0; w < VPL; ++w) {
-        float4 r = acc[w];
-        if (add) V::add(r, V::ld(dst + 128 * w));
-        V::st_stream(dst + 128 * w, r);
+        for (int w = 0; w < VPL; ++w) {
+          float4 r = acc[w];
+          if (add) V::add(r, V::ld(dst + 128 * w));
+          V::st_stream(dst + 128 * w, r);
+        }
       }
     }
   };
+  auto next_row = [&]() {
+    ++lr;
+    if (lr - w0 == 32) {
+      w0 = lr;
+      load_window();
+    }
+    const int j = (int)(lr - w0);
+    rend = __shfl_sync(0xffffffffu, w_end, j);
+    row = __shfl_sync(0xffffffffu, w_out, j);
+    touched = false;
+#pragma unroll
+    for (int w = 0; w < VPL; ++w) acc[w] = V::zero();
+  };
 
-  for (int64_t base = s; base < e; base += U) {
-    int c[U];
-    float v[U];
+  // two register sets of (column, value) pairs and B rows, used alternately by even and odd
+  // steps (compile-time indices, so the arrays stay in registers)
+  int c[2][U];
+  float v[2][U];
+  float4 b[2][U][VPL];
+  auto load_a = [&](auto kc, int64_t base) {  // reads stay inside the padded arrays
+    constexpr int K = decltype(kc)::value;
 #pragma unroll
     for (int q = 0; q < U / 4; ++q) {
       const int4 c4 = ldg_uniform_i4(a.cols + base + 4 * q);
       const float4 v4 = ldg_uniform_f4(a.vals + base + 4 * q);
-      c[4 * q] = c4.x, c[4 * q + 1] = c4.y, c[4 * q + 2] = c4.z, c[4 * q + 3] = c4.w;
-      v[4 * q] = v4.x, v[4 * q + 1] = v4.y, v[4 * q + 2] = v4.z, v[4 * q + 3] = v4.w;
+      c[K][4 * q] = c4.x, c[K][4 * q + 1] = c4.y, c[K][4 * q + 2] = c4.z, c[K][4 * q + 3] = c4.w;
+      v[K][4 * q] = v4.x, v[K][4 * q + 1] = v4.y, v[K][4 * q + 2] = v4.z, v[K][4 * q + 3] = v4.w;
     }
-    float4 b[U][VPL];
+  };
+  auto load_b = [&](auto kc, int64_t base) {
+    constexpr int K = decltype(kc)::value;
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const float *brow = a.B + (int64_t)c[u] * a.ldb + col0;
+      const float *brow = a.B + (int64_t)c[K][u] * a.ldb + col0;
 #pragma unroll
-      for (int w = 0; w < VPL; ++w) b[u][w] = base + u < e ? V::ldg(brow + 128 * w, pol) : V::zero();
+      for (int w = 0; w < VPL; ++w) b[K][u][w] = base + u < e ? V::ldg(brow + 128 * w, pol) : V::zero();
     }
+  };
+  // one step of U nonzeros at `base`, using register set K: request the next step's B rows
+  // and the pairs two steps ahead, then do this step's FMAs
+  auto step = [&](auto kc, int64_t base) {
+    constexpr int K = decltype(kc)::value;
+    load_b(std::integral_constant<int, K ^ 1>(), base + U);  // predicated off past the chunk
+    float vc[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) vc[u] = v[K][u];
+    if (base + 2 * U < e) load_a(kc, base + 2 * U);
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int64_t p = base + u;
       if (p < e) {
         while (p >= rend) {  // warp-uniform: the chunk moves on to a later listed row
           flush(lr == head_lr ? head : -1);
-          ++lr;
-          rend = __ldg(a.lrow_ptr + lr + 1);
-          touched = false;
-#pragma unroll
-          for (int w = 0; w < VPL; ++w) acc[w] = V::zero();
+          next_row();
         }
 #pragma unroll
-        for (int w = 0; w < VPL; ++w) V::fma(acc[w], v[u], b[u][w]);
+        for (int w = 0; w < VPL; ++w) V::fma(acc[w], vc[u], b[K][u][w]);
         touched = true;
       }
     }
+  };
+  const std::integral_constant<int, 0> even;
+  const std::integral_constant<int, 1> odd;
+  load_a(even, s);
+  load_b(even, s);
+  load_a(odd, s + U);
+  for (int64_t base = s; base < e; base += 2 * U) {
+    step(even, base);
+    if (base + U < e) step(odd, base + U);
   }
   flush(tail_slot >= 0 ? tail_slot : (lr == head_lr ? head : -1));
   // the last chunk writes the listed rows after its last nonzero (all empty)
   if (!kAccum && a.zero_rows > 0 && chunk == a.n_chunks - 1) {
-    touched = false;
-#pragma unroll
-    for (int w = 0; w < VPL; ++w) acc[w] = V::zero();
-    for (++lr; lr < a.n_lrows; ++lr) flush(-1);
+    while (lr + 1 < a.n_lrows) {
+      next_row();
+      flush(-1);
+    }
   }
 }
 
@@ -566,7 +615,7 @@ KernelFn select_kernel(int variant, int W, bool accum, int LPR, int VPL) {
 bool aligned(const void *p, uintptr_t bytes) { return ((uintptr_t)p & (bytes - 1)) == 0; }
 
 // Warp-per-chunk shapes (vectors of 4 floats per lane per 128 columns, nonzeros per step).
-#define DSP_WARP_SHAPES(X) X(1, 4) X(1, 8) X(1, 16) X(2, 4) X(2, 8) X(4, 4)
+#define DSP_WARP_SHAPES(X) X(1, 4) X(1, 8) X(2, 4) X(4, 4)
 
 KernelFn warp_kernel_for(int VPL, int U, bool accum) {
 #define DSP_WK(P, Q) \
@@ -601,7 +650,7 @@ WarpShape warp_shape(int N, const float *B, int64_t ldb, const float *C, int64_t
   const int n128 = N / 128;
   int vpl = n128 % 4 == 0 ? 4 : n128 % 2 == 0 ? 2 : 1;
   if (env_vpl > 0 && n128 % env_vpl == 0) vpl = env_vpl;
-  int u = vpl == 1 ? 8 : 4;
+  int u = 4;
   if (env_u > 0) u = env_u;
   if (!warp_kernel_for(vpl, u, false)) return w;
   w.VPL = vpl;
