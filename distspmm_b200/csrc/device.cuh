@@ -8,6 +8,10 @@
 namespace dsp {
 
 constexpr int kSpmmThreads = 256;
+// Diagonal (DIA) form of banded operands: at most kMaxDiag distinct offsets col - row,
+// blocks of kDiaRows consecutive rows per warp (one presence byte per block and diagonal).
+constexpr int kMaxDiag = 32;
+constexpr int kDiaRows = 8;
 
 // The two SpMM work decompositions (picked per operand from its row-length statistics).
 enum SpmmVariant : int {
@@ -50,6 +54,13 @@ struct SpmmArgs {
   // written otherwise; nullptr = every row written (or accumulated, per the launch)
   const uint8_t *first_phase;
   int phase;
+  // row-split operands that are banded: the diagonal form (nullptr when the operand has none)
+  const float *dia_vals;    // [n_diag][dia_m] value of (row i, col i + diag_off[d]), 0 if absent
+  const uint8_t *dia_pres;  // [ceil(dia_m / kDiaRows)][n_diag] bit r: row 8b + r has that entry
+  int64_t dia_m;            // listed rows (consecutive output rows from dia_row0)
+  int64_t dia_row0;
+  int n_diag;
+  int32_t diag_off[kMaxDiag];  // ascending
 };
 
 struct SpmmShape {
@@ -103,6 +114,13 @@ struct DevOperand {
   int32_t *d_split_ptr = nullptr;
   int32_t *d_cols = nullptr;
   float *d_vals = nullptr;
+  // diagonal form (row-split operands whose listed rows are consecutive and that have at
+  // most kMaxDiag distinct offsets, densely filled)
+  float *d_dia_vals = nullptr;
+  uint8_t *d_dia_pres = nullptr;
+  int64_t dia_row0 = 0;
+  int n_diag = 0;
+  int32_t diag_off[kMaxDiag] = {};
 
   // Rows i < m with nonzeros [row_ptr[i], row_ptr[i+1]) of indices/values (offsets are
   // absolute; first_nz is subtracted); row_ids[i] is the output row (nullptr = i).

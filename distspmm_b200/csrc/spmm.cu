@@ -507,6 +507,79 @@ __global__ void __launch_bounds__(kSpmmThreads) spmm_warp_kernel(const SpmmArgs 
   }
 }
 
+// ------------------------------------------------------------------ banded operands (diagonals)
+
+// One block of kDiaRows (8) consecutive rows per warp, on the diagonal form: row i holds
+// the entries (i, i + diag_off[d]). Offsets that follow one another (o, o+1, ..., a run of
+// up to 4, e.g. the x-neighbours of a stencil) share B rows: the 8 rows of a block need
+// B rows jb + k, k < 8 + L - 1, of a run of length L, and each such row is read once and
+// applied to every row r = k - l of the block it touches, so a 27-point stencil reads about
+// 11 B rows per output row instead of 27, and no column ids. Presence bits (one byte per
+// block and diagonal) mark the entries that exist: a B row no entry of the block uses is
+// not read and an absent entry adds nothing, so the result is the CSR product exactly (an
+// explicit zero in A counts as present). Lane l holds output columns col0 .. col0 + 3,
+// blockIdx.y selecting a block of 128 columns. Needs N % 128 == 0 and 16-byte aligned B / C
+// rows.
+template <bool kAccum>
+__global__ void __launch_bounds__(kSpmmThreads) spmm_dia_kernel(const SpmmArgs a) {
+  constexpr int R = kDiaRows;
+  using V = Vec<4>;
+  const unsigned full = 0xffffffffu;
+  const int lane = threadIdx.x & 31;
+  const int64_t blk = ((int64_t)blockIdx.x * kSpmmThreads + threadIdx.x) >> 5;
+  const int64_t i0 = blk * R;
+  if (i0 >= a.dia_m) return;
+  const int col0 = blockIdx.y * 128 + lane * 4;
+  const int64_t orow0 = a.dia_row0 + i0;
+  const uint64_t pol = evict_last_policy();
+  // lane d holds the presence bits of diagonal d for the 8 rows of this block
+  const uint32_t pbyte = lane < a.n_diag ? __ldg(a.dia_pres + blk * a.n_diag + lane) : 0u;
+  float4 acc[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) acc[r] = V::zero();
+
+  for (int d0 = 0; d0 < a.n_diag;) {
+    int L = 1;  // run of consecutive offsets from d0 (warp-uniform)
+    while (d0 + L < a.n_diag && L < 4 && a.diag_off[d0 + L] == a.diag_off[d0] + L) ++L;
+    // lane t = l * 8 + r holds the value of (row i0 + r, diagonal d0 + l)
+    const int tl = lane / R, tr = lane % R;
+    const uint32_t pb = __shfl_sync(full, pbyte, min(d0 + tl, 31));
+    const bool pres = tl < L && ((pb >> tr) & 1u);
+    const float myv = pres ? __ldg(a.dia_vals + (int64_t)(d0 + tl) * a.dia_m + i0 + tr) : 0.f;
+    const uint32_t pm = __ballot_sync(full, pres);
+    const int64_t jb = orow0 + a.diag_off[d0];  // B row of k = 0
+    float4 b[R + 3];
+#pragma unroll
+    for (int k = 0; k < R + 3; ++k) {
+      uint32_t need = 0;  // some present entry of the block uses B row jb + k
+#pragma unroll
+      for (int l = 0; l < 4; ++l)
+        if (k - l >= 0 && k - l < R) need |= (pm >> (l * R + k - l)) & 1u;
+      b[k] = need ? V::ldg(a.B + (jb + k) * a.ldb + col0, pol) : V::zero();
+    }
+#pragma unroll
+    for (int k = 0; k < R + 3; ++k)
+#pragma unroll
+      for (int l = 0; l < 4; ++l) {
+        const int r = k - l;
+        if (r >= 0 && r < R) {
+          const float v = __shfl_sync(full, myv, l * R + r);
+          if ((pm >> (l * R + r)) & 1u) V::fma(acc[r], v, b[k]);
+        }
+      }
+    d0 += L;
+  }
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    if (i0 + r >= a.dia_m) break;
+    const int32_t row = (int32_t)(orow0 + r);
+    float *dst = a.C + (int64_t)row * a.ldc + col0;
+    float4 out = acc[r];
+    if (accumulates<kAccum>(a, row)) V::add(out, V::ld(dst));
+    V::st_stream(dst, out);
+  }
+}
+
 // ------------------------------------------------------------------ fixup and fills
 
 // One warp per cut row: C[row] = (accumulating ? C[row] : 0) + sum of its partial slots,
@@ -729,7 +802,20 @@ int launch_spmm(const SpmmArgs &a, bool accumulate, cudaStream_t stream) {
   const WarpShape ws = a.variant == kNnzSplit && a.lrow_ptr && a.chunk_lrow && a.chunk_nnz % kWarpChunkAlign == 0
                            ? warp_shape(a.N, a.B, a.ldb, a.C, a.ldc)
                            : WarpShape();
-  if (units > 0 && ws.VPL > 0) {
+  // banded row-split operands: the diagonal kernel (DSP_SPMM_DIA=0 turns it off)
+  static const int env_dia = [] {
+    const char *e = getenv("DSP_SPMM_DIA");
+    return e ? atoi(e) : 1;
+  }();
+  const bool dia = env_dia && a.variant == kRowSplit && a.dia_vals && a.dia_m > 0 && a.N % 128 == 0 &&
+                   a.ldb % 4 == 0 && a.ldc % 4 == 0 && aligned(a.B, 16) && aligned(a.C, 16);
+  if (dia) {
+    const int64_t blocks = (a.dia_m + kDiaRows - 1) / kDiaRows;
+    const int64_t gx = (blocks + kSpmmThreads / 32 - 1) / (kSpmmThreads / 32);
+    if (gx > INT32_MAX) return fail(DSP_ERR_UNSUPPORTED, "spmm: %lld row blocks", (long long)blocks);
+    KernelFn k = accumulate ? spmm_dia_kernel<true> : spmm_dia_kernel<false>;
+    k<<<dim3((unsigned)gx, (unsigned)(a.N / 128)), kSpmmThreads, 0, stream>>>(a);
+  } else if (units > 0 && ws.VPL > 0) {
     KernelFn k = warp_kernel_for(ws.VPL, ws.U, accumulate);
     const int64_t gx = (units + kSpmmThreads / 32 - 1) / (kSpmmThreads / 32);
     if (gx > INT32_MAX) return fail(DSP_ERR_UNSUPPORTED, "spmm: %lld work units", (long long)units);
@@ -746,7 +832,7 @@ int launch_spmm(const SpmmArgs &a, bool accumulate, cudaStream_t stream) {
                                       (size_t)a.zero_rows, stream);
     if (e != cudaSuccess) return fail(DSP_ERR_CUDA, "spmm zero fill: %s", cudaGetErrorString(e));
   }
-  if (a.n_split > 0) {
+  if (a.n_split > 0 && !dia) {
     KernelFn f = s.W >= 4 ? (accumulate ? spmm_fixup_kernel<4, true> : spmm_fixup_kernel<4, false>)
                           : (accumulate ? spmm_fixup_kernel<1, true> : spmm_fixup_kernel<1, false>);
     const int64_t gx = (a.n_split * 32 + kSpmmThreads - 1) / kSpmmThreads;
@@ -812,6 +898,74 @@ int64_t wave_chunk_nnz(int device, int dims, int64_t nnz) {
   return (len + kWarpChunkAlign - 1) / kWarpChunkAlign * kWarpChunkAlign;
 }
 
+// The diagonal form of listed rows [0, m) when they are consecutive output rows
+// (row0 + i) and banded: at most kMaxDiag distinct offsets col - row, filling at least
+// half of the m x n_diag entries, no column twice in a row. dv[d * m + i] is the value of
+// (i, row0 + i + offs[d]) (0 if absent) and bit i % 8 of pres[(i / 8) * n_diag + d] says
+// whether the entry exists. Returns false when the operand is not of that shape.
+static bool dia_form(int64_t m, const int32_t *row_ids, const int64_t *rp, const int64_t *idx, const float *val,
+                     int64_t *row0_out, std::vector<int32_t> *offs, std::vector<float> *dv,
+                     std::vector<uint8_t> *pres) {
+  static const int env_dia = [] {
+    const char *e = getenv("DSP_SPMM_DIA");
+    return e ? atoi(e) : 1;
+  }();
+  const int64_t nnz = m > 0 ? rp[m] : 0;
+  if (!env_dia || m <= 0 || nnz <= 0) return false;
+  const int64_t row0 = row_ids ? row_ids[0] : 0;
+  std::atomic<bool> ok{true};
+  if (row_ids)
+    parallel_for(m, [&](int64_t b, int64_t e) {
+      for (int64_t i = b; i < e && ok.load(std::memory_order_relaxed); ++i)
+        if (row_ids[i] != row0 + i) ok = false;
+    }, 1 << 16);
+  if (!ok) return false;
+  // distinct offsets, per host thread then merged
+  std::mutex mu;
+  std::vector<int64_t> all;
+  parallel_for(m, [&](int64_t b, int64_t e) {
+    std::vector<int64_t> mine;
+    for (int64_t i = b; i < e && ok.load(std::memory_order_relaxed); ++i)
+      for (int64_t j = rp[i]; j < rp[i + 1]; ++j) {
+        const int64_t o = idx[j] - (row0 + i);
+        if (std::find(mine.begin(), mine.end(), o) == mine.end()) {
+          mine.push_back(o);
+          if ((int)mine.size() > kMaxDiag) {
+            ok = false;
+            break;
+          }
+        }
+      }
+    std::lock_guard<std::mutex> lk(mu);
+    all.insert(all.end(), mine.begin(), mine.end());
+  }, 1 << 14);
+  if (!ok) return false;
+  std::sort(all.begin(), all.end());
+  all.erase(std::unique(all.begin(), all.end()), all.end());
+  const int nd = (int)all.size();
+  if (nd > kMaxDiag || 2 * nnz < m * (int64_t)nd) return false;
+  offs->assign(all.begin(), all.end());
+  dv->assign((size_t)(m * nd), 0.f);
+  const int64_t nblk = (m + kDiaRows - 1) / kDiaRows;
+  pres->assign((size_t)(nblk * nd), 0);
+  parallel_for(nblk, [&](int64_t b, int64_t e) {
+    for (int64_t blk = b; blk < e; ++blk)
+      for (int64_t i = blk * kDiaRows; i < std::min(m, (blk + 1) * kDiaRows); ++i)
+        for (int64_t j = rp[i]; j < rp[i + 1]; ++j) {
+          const int64_t o = idx[j] - (row0 + i);
+          const int d = (int)(std::lower_bound(all.begin(), all.end(), o) - all.begin());
+          uint8_t &byte = (*pres)[(size_t)(blk * nd + d)];
+          const uint8_t bit = (uint8_t)(1u << (i % kDiaRows));
+          if (byte & bit) ok = false;  // the same column twice in a row
+          byte |= bit;
+          (*dv)[(size_t)(d * m + i)] = val[j];
+        }
+  }, 1024);
+  if (!ok) return false;
+  *row0_out = row0;
+  return true;
+}
+
 int DevOperand::upload(int device_, int64_t rows_, int64_t cols_, const int64_t *row_ptr, const int32_t *row_ids,
                        int64_t m, const int64_t *indices, const float *values, int64_t first_nz, int64_t nnz_,
                        int dims, bool include_empty, int variant_) {
@@ -838,6 +992,17 @@ int DevOperand::upload(int device_, int64_t rows_, int64_t cols_, const int64_t 
     if ((rc = dev_upload(&d_item_ptr, plan.item_ptr.data(), sizeof(int64_t) * plan.item_ptr.size())) ||
         (rc = dev_upload(&d_item_out, plan.item_out.data(), sizeof(int32_t) * plan.item_out.size())))
       return rc;
+    std::vector<int32_t> offs;
+    std::vector<float> dv;
+    std::vector<uint8_t> pres;
+    if (dia_form(m, row_ids, rp.data(), indices + first_nz, values + first_nz, &dia_row0, &offs, &dv, &pres)) {
+      n_diag = (int)offs.size();
+      for (int d = 0; d < n_diag; ++d) diag_off[d] = offs[(size_t)d];
+      n_lrows = m;
+      if ((rc = dev_upload(&d_dia_vals, dv.data(), sizeof(float) * dv.size())) ||
+          (rc = dev_upload(&d_dia_pres, pres.data(), pres.size())))
+        return rc;
+    }
   } else {
     ChunkPlan plan;
     build_chunks(m, row_ids, rp.data(), wave_chunk_nnz(device_, dims, nnz_), &plan);
@@ -878,19 +1043,22 @@ int DevOperand::upload(int device_, int64_t rows_, int64_t cols_, const int64_t 
 
 void DevOperand::release() {
   for (void **p : {(void **)&d_item_ptr, (void **)&d_item_out, (void **)&d_coo_row, (void **)&d_chunk_slot,
-                   (void **)&d_chunk_lrow, (void **)&d_lrow_ptr, (void **)&d_lrow_out, (void **)&d_split_row,
+                   (void **)&d_chunk_lrow, (void **)&d_lrow_ptr, (void **)&d_lrow_out, (void **)&d_dia_vals,
+                   (void **)&d_dia_pres, (void **)&d_split_row,
                    (void **)&d_split_ptr, (void **)&d_cols, (void **)&d_vals}) {
     if (*p) cudaFree(*p);
     *p = nullptr;
   }
   n_items = n_chunks = n_split = pieces = n_lrows = 0;
+  n_diag = 0;
 }
 
 int64_t DevOperand::device_bytes() const {
   const int64_t nnz_split = variant == kNnzSplit
                                 ? nnz * 4 + n_chunks * 4 + (n_lrows + 1) * 8 + (d_lrow_out ? n_lrows * 4 : 0)
                                 : 0;
-  return n_items * 12 + 8 + n_chunks * 8 + nnz_split + n_split * 8 + 4 + (nnz + kWarpChunkPad) * 8;
+  const int64_t dia = d_dia_vals ? n_lrows * n_diag * 4 + (n_lrows + kDiaRows - 1) / kDiaRows * n_diag : 0;
+  return n_items * 12 + 8 + n_chunks * 8 + nnz_split + n_split * 8 + 4 + (nnz + kWarpChunkPad) * 8 + dia;
 }
 
 SpmmArgs DevOperand::args(const float *B, int64_t ldb, float *C, int64_t ldc, int N, float *partial) const {
@@ -906,6 +1074,12 @@ SpmmArgs DevOperand::args(const float *B, int64_t ldb, float *C, int64_t ldc, in
   a.lrow_out = d_lrow_out;
   a.chunk_lrow = d_chunk_lrow;
   a.n_lrows = n_lrows;
+  a.dia_vals = d_dia_vals;
+  a.dia_pres = d_dia_pres;
+  a.dia_m = d_dia_vals ? n_lrows : 0;
+  a.dia_row0 = dia_row0;
+  a.n_diag = n_diag;
+  memcpy(a.diag_off, diag_off, sizeof diag_off);
   a.n_chunks = n_chunks;
   a.chunk_nnz = chunk_nnz;
   a.nnz = nnz;

@@ -204,3 +204,70 @@ def test_agrees_with_cusparse(gpu, kind, kw, N):
     Cs = (At @ torch.from_numpy(B).cuda()).cpu().numpy()
     _, ab = oracle.spmm_f64(A.indptr, A.indices, A.values, B)
     assert np.all(np.abs(C - Cs) <= 2 * RTOL * ab + 1e-30), float(np.max(np.abs(C - Cs) / (ab + 1e-30)))
+
+
+def _banded(m, offsets, keep, seed):
+    """m x m matrix with entries (i, i + o) for o in offsets where keep(i, o), values U(0.5, 1)."""
+    rng = np.random.default_rng(seed)
+    ip, ix = [0], []
+    for i in range(m):
+        cols = [i + o for o in offsets if 0 <= i + o < m and keep(i, o)]
+        ix.extend(cols)
+        ip.append(len(ix))
+    vals = rng.uniform(0.5, 1.0, len(ix)).astype(np.float32)
+    return d.Csr(np.array(ip, np.int64), np.array(ix, np.int64), vals, m, m)
+
+
+def test_banded_diagonal_kernel_absent_entries_read_nothing(gpu):
+    """Banded operands run on the diagonal kernel. An entry that does not exist must not
+    read B: B rows that no entry uses hold NaN, and C must stay finite and match the
+    oracle. Rows near the matrix edges, rows without entries, and row counts that are not
+    a multiple of the 8-row blocks are included."""
+    import torch
+    from distspmm_b200.spmm import SpmmPlan
+    m, N = 1003, 128
+    # offsets -2..2 (one run) and +-100 (single diagonals); column 500 and 777 are never used
+    A = _banded(m, [-100, -2, -1, 0, 1, 2, 100],
+                lambda i, o: i + o not in (500, 777) and i % 97 != 13, seed=3)
+    B = d.dense_b(m, N, 5)
+    B[[500, 777]] = np.nan
+    plan = SpmmPlan(A, 0, N)
+    assert plan.info()["variant"] == 0
+    C = plan(torch.from_numpy(B).cuda()).cpu().numpy()
+    assert np.isfinite(C).all()
+    Bz = B.copy()
+    Bz[[500, 777]] = 0
+    ref, ab = oracle.spmm_f64(A.indptr, A.indices, A.values, Bz)
+    ok, worst = oracle.check_close(C, ref, ab, RTOL)
+    assert ok, worst
+    # accumulate: C += A.B
+    C0 = d.dense_b(m, N, 9)
+    C2 = plan(torch.from_numpy(B).cuda(), torch.from_numpy(C0.copy()).cuda(), accumulate=True).cpu().numpy()
+    ok, worst = oracle.check_close(C2, ref + C0, ab + np.abs(C0), RTOL)
+    assert ok, worst
+
+
+def test_banded_explicit_zero_still_reads_its_b_row(gpu):
+    """An explicit 0.0 in A is an entry: its B row is read, so a NaN there gives NaN in C,
+    exactly as the CSR product (and the oracle) gives."""
+    import torch
+    from distspmm_b200.spmm import SpmmPlan
+    m, N = 64, 128
+    A = _banded(m, [-1, 0, 1], lambda i, o: True, seed=4)
+    row, col = 10, 11  # entry (10, 11)
+    k = int(np.nonzero(A.indices[A.indptr[row]:A.indptr[row + 1]] == col)[0][0]) + int(A.indptr[row])
+    A.values[k] = 0.0
+    B = d.dense_b(m, N, 6)
+    B[col] = np.nan
+    C = SpmmPlan(A, 0, N)(torch.from_numpy(B).cuda()).cpu().numpy()
+    nan_rows = sorted(set(np.nonzero(~np.isfinite(C))[0].tolist()))
+    assert nan_rows == [10, 11, 12]  # every row with an entry in column 11, the zero included
+
+
+def test_stencil_diagonal_kernel_widths(gpu):
+    """The 27-point stencil (the banded benchmark matrix) at several widths: N = 128 and 256
+    use the diagonal kernel, N = 64 and 100 the row kernels; all match the oracle."""
+    A = d.gen_stencil27(14, seed=7)
+    for N in (64, 100, 128, 256):
+        B, C, plan = _run(A, N)
+        _check(A, B, C)
