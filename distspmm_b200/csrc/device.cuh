@@ -33,11 +33,6 @@ struct SpmmArgs {
   int64_t chunk_nnz;
   int64_t nnz;
   int64_t zero_rows;  // rows [0, zero_rows) without nonzeros are written as 0 (non-accumulating)
-  // nnz-split, warp-per-chunk kernel: the operand's listed rows instead of per-nonzero ids
-  const int64_t *lrow_ptr;    // [n_lrows + 1] nonzero range of each listed row
-  const int32_t *lrow_out;    // [n_lrows] output row of each listed row (nullptr = identity)
-  const int32_t *chunk_lrow;  // [n_chunks] first listed row of each chunk
-  int64_t n_lrows;
   // both: rows cut across items / chunks, summed into C by the fixup kernel
   const int32_t *split_row;  // [n_split]
   const int32_t *split_ptr;  // [n_split + 1] slot ranges
@@ -74,13 +69,6 @@ struct SpmmShape {
 // max_w caps the vector width for kernels instantiated only up to float4.
 SpmmShape spmm_shape(int N, int variant, const float *B, int64_t ldb, const float *C, int64_t ldc,
                      int max_w = 8);
-// Entries the cols / vals arrays of an nnz-split operand are padded with (zeros): the
-// warp-per-chunk kernel reads the (column, value) pairs of up to this many nonzeros at once
-// with vector loads that may run past a chunk's end.
-constexpr int kWarpChunkPad = 16;
-// Chunk lengths of the warp-per-chunk kernel are multiples of this (16-byte aligned
-// vector loads of the column ids and values).
-constexpr int kWarpChunkAlign = 16;
 int launch_spmm(const SpmmArgs &a, bool accumulate, cudaStream_t stream);
 int launch_fill_dense(float *B, int64_t row0, int64_t rows, int64_t ld, int64_t ncols, uint64_t seed,
                       cudaStream_t stream);
@@ -106,10 +94,7 @@ struct DevOperand {
   int32_t *d_item_out = nullptr;
   int32_t *d_coo_row = nullptr;
   int32_t *d_chunk_slot = nullptr;
-  int64_t *d_lrow_ptr = nullptr;
-  int32_t *d_lrow_out = nullptr;
-  int32_t *d_chunk_lrow = nullptr;
-  int64_t n_lrows = 0;
+  int64_t n_lrows = 0;  // rows the operand lists (the diagonal form's row count)
   int32_t *d_split_row = nullptr;
   int32_t *d_split_ptr = nullptr;
   int32_t *d_cols = nullptr;

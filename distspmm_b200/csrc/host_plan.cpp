@@ -437,7 +437,6 @@ void build_chunks(int64_t m, const int32_t *rows, const int64_t *row_ptr, int64_
   out->n_chunks = (nnz + chunk_nnz - 1) / chunk_nnz;
   out->coo_row.assign((size_t)std::max<int64_t>(nnz, 1), 0);
   out->chunk_slot.assign((size_t)std::max<int64_t>(2 * out->n_chunks, 1), -1);
-  out->chunk_lrow.assign((size_t)std::max<int64_t>(out->n_chunks, 1), 0);
   out->split_row.clear();
   out->split_ptr.assign(1, 0);
   std::atomic<int64_t> maxlen{0};
@@ -471,9 +470,6 @@ void build_chunks(int64_t m, const int32_t *rows, const int64_t *row_ptr, int64_
     const int64_t hr = row_of(s), tr = row_of(e - 1);
     const bool head_cut = row_ptr[hr] < s;        // the row began in an earlier chunk
     const bool tail_cut = row_ptr[tr + 1] > e;    // the row goes on in a later chunk
-    // first listed row chunk c walks: the row it continues, else the row after the previous
-    // chunk's last one (listed rows without nonzeros in between are the chunk's to write)
-    out->chunk_lrow[(size_t)c] = c == 0 ? 0 : (int32_t)(head_cut ? hr : row_of(s - 1) + 1);
     if (hr == tr) {
       if (head_cut || tail_cut) out->chunk_slot[(size_t)(2 * c)] = out->chunk_slot[(size_t)(2 * c + 1)] = add_slot(hr);
     } else {

@@ -55,12 +55,9 @@ void build_items(int64_t m, const int32_t *rows, const int64_t *row_ptr, int64_t
 //   chunk_slot[2c+0/1]   partial slot of chunk c's first / last row when that row crosses a
 //                        chunk boundary, -1 when the chunk holds the whole row
 //   split_row/split_ptr  rows crossing boundaries and their consecutive slots (chunk order)
-//   chunk_lrow[c]        first listed row (index into row_ptr) chunk c walks: the row it
-//                        continues, else the row after the previous chunk's last row
 struct ChunkPlan {
   std::vector<int32_t> coo_row;
   std::vector<int32_t> chunk_slot;
-  std::vector<int32_t> chunk_lrow;
   std::vector<int32_t> split_row;
   std::vector<int32_t> split_ptr;
   int64_t chunk_nnz = 0;

@@ -27,7 +27,6 @@
 #include <string.h>
 
 #include <mutex>
-#include <type_traits>
 
 #include "device.cuh"
 #include "internal.h"
@@ -346,35 +345,19 @@ __global__ void __launch_bounds__(kSpmmThreads) spmm_nnz_kernel(const SpmmArgs a
 
 // ------------------------------------------------------------------ nnz-split, warp per chunk
 
-// (column, value) pairs of 4 consecutive nonzeros, read by every lane of the warp from the
-// same 16-byte address (one L1 wavefront each, served to all lanes).
-__device__ __forceinline__ int4 ldg_uniform_i4(const int32_t *p) {
-  int4 v;
-  asm("ld.global.nc.L1::evict_last.v4.s32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
-  return v;
-}
-__device__ __forceinline__ float4 ldg_uniform_f4(const float *p) {
-  float4 v;
-  asm("ld.global.nc.L1::evict_last.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
-  return v;
-}
-
 // One chunk of chunk_nnz consecutive nonzeros per warp; lane l holds output columns
 // col0 + 128 v .. +3 (v < VPL) of the current row, blockIdx.y selecting a block of
-// 128 * VPL columns. The chunk is walked U nonzeros per step, software-pipelined: the
-// (column, value) pairs of step i + 2 are read (uniform vector loads) and the U B rows of
-// step i + 1 are requested (one 512-byte row per warp instruction at VPL = 1) before the
-// FMAs of step i, so 2U row loads are in flight behind the arithmetic. Rows are the
-// operand's listed rows; the boundaries and output rows of 32 consecutive listed rows sit
-// one per lane (read once per 32 rows), so a row change costs two shuffles and no memory
-// wait, and is the same for every lane (no divergence). Listed rows without nonzeros that
-// a chunk walks past are written as zeros (non-accumulating launches); cut rows go to
-// their partial slots as in spmm_nnz_kernel. Needs N % (128 * VPL) == 0, 16-byte aligned
-// B / C rows, chunk_nnz a multiple of kWarpChunkAlign and cols / vals padded by
-// kWarpChunkPad entries.
-template <int VPL, int U, bool kAccum>
-__global__ void __launch_bounds__(kSpmmThreads) spmm_warp_kernel(const SpmmArgs a) {
-  static_assert(U % 4 == 0 && 2 * U <= kWarpChunkPad && kWarpChunkAlign % U == 0, "U");
+// 128 * VPL columns. Each step reads the column, value and output row of U nonzeros (every
+// lane reads the same words: one request each, served to the whole warp), then requests
+// their U B rows (one 512-byte row per warp instruction at VPL = 1) and does the FMAs. A
+// row change is met when the next nonzero's row id differs, which is the same for every
+// lane, so no lane diverges; the finished row is written (to its partial slot when it is
+// cut by a chunk boundary, as in spmm_nnz_kernel). No loads are carried across steps: with
+// few registers per lane, many warps per SM keep the B rows in flight instead (measured on
+// B200 against software-pipelined and lane-group forms of the same loop: 1.06 / 1.68 /
+// 1.43 ms on the R-MAT scale-20 stream).
+template <int VPL, int U, bool kAccum, int kMinBlocks>
+__global__ void __launch_bounds__(kSpmmThreads, kMinBlocks) spmm_warp_kernel(const SpmmArgs a) {
   using V = Vec<4>;
   const int lane = threadIdx.x & 31;
   const int64_t chunk = ((int64_t)blockIdx.x * kSpmmThreads + threadIdx.x) >> 5;
@@ -384,127 +367,65 @@ __global__ void __launch_bounds__(kSpmmThreads) spmm_warp_kernel(const SpmmArgs 
   const int32_t head_slot = a.chunk_slot[2 * chunk], tail_slot = a.chunk_slot[2 * chunk + 1];
   const uint64_t pol = evict_last_policy();
 
-  // window of listed rows [w0, w0 + 32): lane j holds the end of row w0 + j and its output row
-  int64_t lr = a.chunk_lrow[chunk];
-  const int64_t head_lr = lr;
-  int64_t w0 = lr;
-  int64_t w_end = 0;
-  int32_t w_out = 0;
-  auto load_window = [&]() {
-    const int64_t r = w0 + lane;
-    w_end = r < a.n_lrows ? __ldg(a.lrow_ptr + r + 1) : INT64_MAX;
-    w_out = r < a.n_lrows ? (a.lrow_out ? __ldg(a.lrow_out + r) : (int32_t)r) : 0;
-  };
-  load_window();
-  int64_t rend = __shfl_sync(0xffffffffu, w_end, 0);
-  int32_t row = __shfl_sync(0xffffffffu, w_out, 0);
-  // the chunk's first row is its head slot's only when that row began in an earlier chunk
-  // (otherwise chunk_lrow may name empty rows before the first row holding a nonzero, and a
-  // single cut row's slot is the tail slot)
-  const int32_t head = __ldg(a.lrow_ptr + lr) < s ? head_slot : -1;
-  bool touched = false;  // the current row received a nonzero of this chunk
+  int32_t row = __ldg(a.coo_row + s);
+  const int32_t head_row = row;
   float4 acc[VPL];
+  // rows [r0, r1) hold no nonzeros: zeros (only operands that list every output row,
+  // zero_rows > 0, own the rows in between)
+  auto zeros = [&](int64_t r0, int64_t r1) {
+    for (int64_t r = r0; r < r1; ++r)
 #pragma unroll
-  for (int w = 0; w < VPL; ++w) acc[w] = V::zero();
-
-  // Write the current row (to its slot, or C); an accumulating launch skips rows that got no
-  // nonzero here, a writing one writes them (their zeros).
+      for (int w = 0; w < VPL; ++w) V::st_stream(a.C + r * a.ldc + col0 + 128 * w, V::zero());
+  };
   auto flush = [&](int32_t slot) {
     if (slot >= 0) {
       float *dst = a.partial + (int64_t)slot * a.N + col0;
 #pragma unroll
       for (int w = 0; w < VPL; ++w) V::st(dst + 128 * w, acc[w]);
     } else {
+      float *dst = a.C + (int64_t)row * a.ldc + col0;
       const bool add = accumulates<kAccum>(a, row);
-      if (!(add && !touched)) {
-        float *dst = a.C + (int64_t)row * a.ldc + col0;
 #pragma unroll
-        for (int w = 0; w < VPL; ++w) {
-          float4 r = acc[w];
-          if (add) V::add(r, V::ld(dst + 128 * w));
-          V::st_stream(dst + 128 * w, r);
-        }
+      for (int w = 0; w < VPL; ++w) {
+        float4 r = acc[w];
+        if (add) V::add(r, V::ld(dst + 128 * w));
+        V::st_stream(dst + 128 * w, r);
       }
     }
   };
-  auto next_row = [&]() {
-    ++lr;
-    if (lr - w0 == 32) {
-      w0 = lr;
-      load_window();
-    }
-    const int j = (int)(lr - w0);
-    rend = __shfl_sync(0xffffffffu, w_end, j);
-    row = __shfl_sync(0xffffffffu, w_out, j);
-    touched = false;
+  if (!kAccum && a.zero_rows > 0) zeros(s > 0 ? (int64_t)__ldg(a.coo_row + s - 1) + 1 : 0, row);
 #pragma unroll
-    for (int w = 0; w < VPL; ++w) acc[w] = V::zero();
-  };
+  for (int w = 0; w < VPL; ++w) acc[w] = V::zero();
 
-  // two register sets of (column, value) pairs and B rows, used alternately by even and odd
-  // steps (compile-time indices, so the arrays stay in registers)
-  int c[2][U];
-  float v[2][U];
-  float4 b[2][U][VPL];
-  auto load_a = [&](auto kc, int64_t base) {  // reads stay inside the padded arrays
-    constexpr int K = decltype(kc)::value;
-#pragma unroll
-    for (int q = 0; q < U / 4; ++q) {
-      const int4 c4 = ldg_uniform_i4(a.cols + base + 4 * q);
-      const float4 v4 = ldg_uniform_f4(a.vals + base + 4 * q);
-      c[K][4 * q] = c4.x, c[K][4 * q + 1] = c4.y, c[K][4 * q + 2] = c4.z, c[K][4 * q + 3] = c4.w;
-      v[K][4 * q] = v4.x, v[K][4 * q + 1] = v4.y, v[K][4 * q + 2] = v4.z, v[K][4 * q + 3] = v4.w;
-    }
-  };
-  auto load_b = [&](auto kc, int64_t base) {
-    constexpr int K = decltype(kc)::value;
+  for (int64_t p = s; p < e; p += U) {
+    float4 b[U][VPL];
+    float v[U];
+    int32_t r[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const float *brow = a.B + (int64_t)c[K][u] * a.ldb + col0;
+      const bool ok = p + u < e;
+      const int32_t c = ok ? __ldg(a.cols + p + u) : 0;
+      v[u] = ok ? __ldg(a.vals + p + u) : 0.f;
+      r[u] = ok ? __ldg(a.coo_row + p + u) : row;
+      const float *brow = a.B + (int64_t)c * a.ldb + col0;
 #pragma unroll
-      for (int w = 0; w < VPL; ++w) b[K][u][w] = base + u < e ? V::ldg(brow + 128 * w, pol) : V::zero();
+      for (int w = 0; w < VPL; ++w) b[u][w] = ok ? V::ldg(brow + 128 * w, pol) : V::zero();
     }
-  };
-  // one step of U nonzeros at `base`, using register set K: request the next step's B rows
-  // and the pairs two steps ahead, then do this step's FMAs
-  auto step = [&](auto kc, int64_t base) {
-    constexpr int K = decltype(kc)::value;
-    load_b(std::integral_constant<int, K ^ 1>(), base + U);  // predicated off past the chunk
-    float vc[U];
-#pragma unroll
-    for (int u = 0; u < U; ++u) vc[u] = v[K][u];
-    if (base + 2 * U < e) load_a(kc, base + 2 * U);
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const int64_t p = base + u;
-      if (p < e) {
-        while (p >= rend) {  // warp-uniform: the chunk moves on to a later listed row
-          flush(lr == head_lr ? head : -1);
-          next_row();
-        }
+      if (r[u] != row) {  // warp-uniform: the chunk crosses into the next row
+        flush(row == head_row ? head_slot : -1);
+        if (!kAccum && a.zero_rows > 0) zeros((int64_t)row + 1, r[u]);
+        row = r[u];
 #pragma unroll
-        for (int w = 0; w < VPL; ++w) V::fma(acc[w], vc[u], b[K][u][w]);
-        touched = true;
+        for (int w = 0; w < VPL; ++w) acc[w] = V::zero();
       }
-    }
-  };
-  const std::integral_constant<int, 0> even;
-  const std::integral_constant<int, 1> odd;
-  load_a(even, s);
-  load_b(even, s);
-  load_a(odd, s + U);
-  for (int64_t base = s; base < e; base += 2 * U) {
-    step(even, base);
-    if (base + U < e) step(odd, base + U);
-  }
-  flush(tail_slot >= 0 ? tail_slot : (lr == head_lr ? head : -1));
-  // the last chunk writes the listed rows after its last nonzero (all empty)
-  if (!kAccum && a.zero_rows > 0 && chunk == a.n_chunks - 1) {
-    while (lr + 1 < a.n_lrows) {
-      next_row();
-      flush(-1);
+#pragma unroll
+      for (int w = 0; w < VPL; ++w) V::fma(acc[w], v[u], b[u][w]);
     }
   }
+  flush(tail_slot >= 0 ? tail_slot : (row == head_row ? head_slot : -1));
+  if (!kAccum && a.zero_rows > 0 && chunk == a.n_chunks - 1) zeros((int64_t)row + 1, a.zero_rows);
 }
 
 // ------------------------------------------------------------------ banded operands (diagonals)
@@ -687,12 +608,13 @@ KernelFn select_kernel(int variant, int W, bool accum, int LPR, int VPL) {
 
 bool aligned(const void *p, uintptr_t bytes) { return ((uintptr_t)p & (bytes - 1)) == 0; }
 
-// Warp-per-chunk shapes (vectors of 4 floats per lane per 128 columns, nonzeros per step).
-#define DSP_WARP_SHAPES(X) X(1, 4) X(1, 8) X(2, 4) X(4, 4)
+// Warp-per-chunk shapes: vectors of 4 floats per lane per 128 columns, nonzeros per step,
+// and the blocks per SM the register allocation is held to (1: the compiler's choice).
+#define DSP_WARP_SHAPES(X) X(1, 2, 1) X(1, 4, 1) X(1, 4, 5) X(1, 8, 1) X(2, 2, 1) X(2, 4, 1) X(4, 2, 1)
 
-KernelFn warp_kernel_for(int VPL, int U, bool accum) {
-#define DSP_WK(P, Q) \
-  if (VPL == P && U == Q) return accum ? spmm_warp_kernel<P, Q, true> : spmm_warp_kernel<P, Q, false>;
+KernelFn warp_kernel_for(int VPL, int U, bool accum, int MB = 1) {
+#define DSP_WK(P, Q, B) \
+  if (VPL == P && U == Q && MB == B) return accum ? spmm_warp_kernel<P, Q, true, B> : spmm_warp_kernel<P, Q, false, B>;
   DSP_WARP_SHAPES(DSP_WK)
 #undef DSP_WK
   return nullptr;
@@ -702,7 +624,7 @@ KernelFn warp_kernel_for(int VPL, int U, bool accum) {
 // lane-group kernels then run): N a multiple of 128, 16-byte aligned rows of B and C.
 // DSP_SPMM_WARP=0 turns it off; DSP_SPMM_WARP_VPL / DSP_SPMM_WARP_U force a shape (sweeps).
 struct WarpShape {
-  int VPL = 0, U = 0, gy = 0;
+  int VPL = 0, U = 0, gy = 0, MB = 1;
 };
 WarpShape warp_shape(int N, const float *B, int64_t ldb, const float *C, int64_t ldc) {
   static const int env_on = [] {
@@ -717,17 +639,23 @@ WarpShape warp_shape(int N, const float *B, int64_t ldb, const float *C, int64_t
     const char *e = getenv("DSP_SPMM_WARP_U");
     return e ? atoi(e) : 0;
   }();
+  static const int env_mb = [] {
+    const char *e = getenv("DSP_SPMM_WARP_MB");
+    return e ? atoi(e) : 1;
+  }();
   WarpShape w;
   if (!env_on || N <= 0 || N % 128 != 0 || ldb % 4 != 0 || ldc % 4 != 0 || !aligned(B, 16) || !aligned(C, 16))
     return w;
   const int n128 = N / 128;
   int vpl = n128 % 4 == 0 ? 4 : n128 % 2 == 0 ? 2 : 1;
   if (env_vpl > 0 && n128 % env_vpl == 0) vpl = env_vpl;
-  int u = 4;
+  int u = vpl == 4 ? 2 : 4;
   if (env_u > 0) u = env_u;
-  if (!warp_kernel_for(vpl, u, false)) return w;
+  const int mb = warp_kernel_for(vpl, u, false, env_mb) ? env_mb : 1;
+  if (!warp_kernel_for(vpl, u, false, mb)) return w;
   w.VPL = vpl;
   w.U = u;
+  w.MB = mb;
   w.gy = n128 / vpl;
   return w;
 }
@@ -799,9 +727,7 @@ int launch_spmm(const SpmmArgs &a, bool accumulate, cudaStream_t stream) {
   const SpmmShape s = spmm_shape(a.N, a.variant, a.B, a.ldb, a.C, a.ldc);
   if (s.chunks > 65535) return fail(DSP_ERR_UNSUPPORTED, "spmm: N = %d too wide", a.N);
   const int64_t units = a.variant == kRowSplit ? a.n_items : a.n_chunks;
-  const WarpShape ws = a.variant == kNnzSplit && a.lrow_ptr && a.chunk_lrow && a.chunk_nnz % kWarpChunkAlign == 0
-                           ? warp_shape(a.N, a.B, a.ldb, a.C, a.ldc)
-                           : WarpShape();
+  const WarpShape ws = a.variant == kNnzSplit ? warp_shape(a.N, a.B, a.ldb, a.C, a.ldc) : WarpShape();
   // banded row-split operands: the diagonal kernel (DSP_SPMM_DIA=0 turns it off)
   static const int env_dia = [] {
     const char *e = getenv("DSP_SPMM_DIA");
@@ -816,7 +742,7 @@ int launch_spmm(const SpmmArgs &a, bool accumulate, cudaStream_t stream) {
     KernelFn k = accumulate ? spmm_dia_kernel<true> : spmm_dia_kernel<false>;
     k<<<dim3((unsigned)gx, (unsigned)(a.N / 128)), kSpmmThreads, 0, stream>>>(a);
   } else if (units > 0 && ws.VPL > 0) {
-    KernelFn k = warp_kernel_for(ws.VPL, ws.U, accumulate);
+    KernelFn k = warp_kernel_for(ws.VPL, ws.U, accumulate, ws.MB);
     const int64_t gx = (units + kSpmmThreads / 32 - 1) / (kSpmmThreads / 32);
     if (gx > INT32_MAX) return fail(DSP_ERR_UNSUPPORTED, "spmm: %lld work units", (long long)units);
     k<<<dim3((unsigned)gx, (unsigned)ws.gy), kSpmmThreads, 0, stream>>>(a);
@@ -883,7 +809,8 @@ int64_t wave_chunk_nnz(int device, int dims, int64_t nnz) {
   const int ld = (dims + 7) & ~7;
   const SpmmShape sh = spmm_shape(dims, kNnzSplit, aligned_ptr, ld, aligned_ptr, ld);
   const WarpShape ws = warp_shape(dims, aligned_ptr, ld, aligned_ptr, ld);
-  KernelFn k = ws.VPL > 0 ? warp_kernel_for(ws.VPL, ws.U, false) : select_kernel(kNnzSplit, sh.W, false, sh.LPR, sh.VPL);
+  KernelFn k = ws.VPL > 0 ? warp_kernel_for(ws.VPL, ws.U, false, ws.MB)
+                          : select_kernel(kNnzSplit, sh.W, false, sh.LPR, sh.VPL);
   const int lanes = ws.VPL > 0 ? 32 : sh.LPR, col_blocks = ws.VPL > 0 ? ws.gy : sh.chunks;
   int sms = 0, per_sm = 0;
   if (!k || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess ||
@@ -895,7 +822,7 @@ int64_t wave_chunk_nnz(int device, int dims, int64_t nnz) {
   const int64_t resident = (int64_t)sms * per_sm * (kSpmmThreads / lanes) / std::max(col_blocks, 1);
   const int64_t waves = std::max<int64_t>(2, (nnz + c * resident - 1) / (c * resident));
   const int64_t len = std::max<int64_t>(8, (nnz + waves * resident - 1) / (waves * resident));
-  return (len + kWarpChunkAlign - 1) / kWarpChunkAlign * kWarpChunkAlign;
+  return len;
 }
 
 // The diagonal form of listed rows [0, m) when they are consecutive output rows
@@ -1013,18 +940,13 @@ int DevOperand::upload(int device_, int64_t rows_, int64_t cols_, const int64_t 
     max_row_len = plan.max_row_len;
     split_row.swap(plan.split_row);
     split_ptr.swap(plan.split_ptr);
-    n_lrows = m;
     if ((rc = dev_upload(&d_coo_row, plan.coo_row.data(), sizeof(int32_t) * (size_t)nnz)) ||
-        (rc = dev_upload(&d_chunk_slot, plan.chunk_slot.data(), sizeof(int32_t) * (size_t)(2 * n_chunks))) ||
-        (rc = dev_upload(&d_chunk_lrow, plan.chunk_lrow.data(), sizeof(int32_t) * (size_t)n_chunks)) ||
-        (rc = dev_upload(&d_lrow_ptr, rp.data(), sizeof(int64_t) * (size_t)(m + 1))) ||
-        (row_ids && (rc = dev_upload(&d_lrow_out, row_ids, sizeof(int32_t) * (size_t)m))))
+        (rc = dev_upload(&d_chunk_slot, plan.chunk_slot.data(), sizeof(int32_t) * (size_t)(2 * n_chunks))))
       return rc;
   }
   n_split = (int64_t)split_row.size();
-  // column ids (int32) and values, padded with kWarpChunkPad zero entries for the vector
-  // reads of the warp-per-chunk kernel
-  const int64_t padded = nnz + kWarpChunkPad;
+  // column ids (int32) and values
+  const int64_t padded = std::max<int64_t>(nnz, 1);
   std::vector<int32_t> c32((size_t)padded, 0);
   std::vector<float> v32((size_t)padded, 0.f);
   parallel_for(nnz, [&](int64_t b, int64_t e) {
@@ -1043,8 +965,7 @@ int DevOperand::upload(int device_, int64_t rows_, int64_t cols_, const int64_t 
 
 void DevOperand::release() {
   for (void **p : {(void **)&d_item_ptr, (void **)&d_item_out, (void **)&d_coo_row, (void **)&d_chunk_slot,
-                   (void **)&d_chunk_lrow, (void **)&d_lrow_ptr, (void **)&d_lrow_out, (void **)&d_dia_vals,
-                   (void **)&d_dia_pres, (void **)&d_split_row,
+                   (void **)&d_dia_vals, (void **)&d_dia_pres, (void **)&d_split_row,
                    (void **)&d_split_ptr, (void **)&d_cols, (void **)&d_vals}) {
     if (*p) cudaFree(*p);
     *p = nullptr;
@@ -1054,11 +975,9 @@ void DevOperand::release() {
 }
 
 int64_t DevOperand::device_bytes() const {
-  const int64_t nnz_split = variant == kNnzSplit
-                                ? nnz * 4 + n_chunks * 4 + (n_lrows + 1) * 8 + (d_lrow_out ? n_lrows * 4 : 0)
-                                : 0;
+  const int64_t nnz_split = variant == kNnzSplit ? nnz * 4 : 0;
   const int64_t dia = d_dia_vals ? n_lrows * n_diag * 4 + (n_lrows + kDiaRows - 1) / kDiaRows * n_diag : 0;
-  return n_items * 12 + 8 + n_chunks * 8 + nnz_split + n_split * 8 + 4 + (nnz + kWarpChunkPad) * 8 + dia;
+  return n_items * 12 + 8 + n_chunks * 8 + nnz_split + n_split * 8 + 4 + nnz * 8 + dia;
 }
 
 SpmmArgs DevOperand::args(const float *B, int64_t ldb, float *C, int64_t ldc, int N, float *partial) const {
@@ -1070,10 +989,6 @@ SpmmArgs DevOperand::args(const float *B, int64_t ldb, float *C, int64_t ldc, in
   a.n_items = n_items;
   a.coo_row = d_coo_row;
   a.chunk_slot = d_chunk_slot;
-  a.lrow_ptr = d_lrow_ptr;
-  a.lrow_out = d_lrow_out;
-  a.chunk_lrow = d_chunk_lrow;
-  a.n_lrows = n_lrows;
   a.dia_vals = d_dia_vals;
   a.dia_pres = d_dia_pres;
   a.dia_m = d_dia_vals ? n_lrows : 0;
@@ -1123,8 +1038,8 @@ void prefer_l1_carveout() {
               cudaFuncSetAttribute(select_kernel(v, w, acc != 0, lpr, vpl),
                                    cudaFuncAttributePreferredSharedMemoryCarveout, 0);
   for (int acc = 0; acc < 2; ++acc) {
-#define DSP_WC(P, Q) \
-  cudaFuncSetAttribute(warp_kernel_for(P, Q, acc != 0), cudaFuncAttributePreferredSharedMemoryCarveout, 0);
+#define DSP_WC(P, Q, B) \
+  cudaFuncSetAttribute(warp_kernel_for(P, Q, acc != 0, B), cudaFuncAttributePreferredSharedMemoryCarveout, 0);
     DSP_WARP_SHAPES(DSP_WC)
 #undef DSP_WC
   }
