@@ -94,7 +94,8 @@ struct DevOperand {
   int32_t *d_item_out = nullptr;
   int32_t *d_coo_row = nullptr;
   int32_t *d_chunk_slot = nullptr;
-  int64_t n_lrows = 0;  // rows the operand lists (the diagonal form's row count)
+  int64_t n_lrows = 0;   // rows the operand lists (the diagonal form's row count)
+  int64_t hot_cols = 0;  // columns whose B rows are read with evict_last (mark_hot_columns)
   int32_t *d_split_row = nullptr;
   int32_t *d_split_ptr = nullptr;
   int32_t *d_cols = nullptr;

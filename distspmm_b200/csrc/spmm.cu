@@ -129,6 +129,20 @@ __device__ __forceinline__ uint64_t evict_last_policy() {
   asm("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
   return pol;
 }
+__device__ __forceinline__ uint64_t evict_first_policy() {
+  uint64_t pol;
+  asm("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+// Stored column ids of CSR operands carry the L2 policy of their B row in bit 31: set for
+// the operand's most-referenced ("hot") columns, whose rows are read with evict_last so that
+// they stay in L2; clear for the others, read with evict_first so that rows used once or
+// twice do not push the hot rows out (mark_hot_columns decides on the host).
+__device__ __forceinline__ int32_t col_id(int32_t stored) { return stored & 0x7fffffff; }
+__device__ __forceinline__ uint64_t col_policy(int32_t stored, uint64_t hot, uint64_t cold) {
+  return stored < 0 ? hot : cold;
+}
 
 template <int LPR>
 __device__ __forceinline__ unsigned group_mask() {
@@ -215,7 +229,7 @@ __global__ void __launch_bounds__(kSpmmThreads) spmm_rows_kernel(const SpmmArgs 
   const unsigned gmask = group_mask<LPR>();
   const int col0 = blockIdx.y * (LPR * VPL * W) + lane * W;
   const int64_t beg = a.item_ptr[item], end = a.item_ptr[item + 1];
-  const uint64_t pol = evict_last_policy();
+  const uint64_t pol_hot = evict_last_policy(), pol_cold = evict_first_policy();
 
   constexpr int K = entries_per_lane<LPR>();
   T acc[VPL];
@@ -241,9 +255,10 @@ __global__ void __launch_bounds__(kSpmmThreads) spmm_rows_kernel(const SpmmArgs 
         float s[U];
 #pragma unroll
         for (int u = 0; u < U; ++u) {
-          const int cj = __shfl_sync(gmask, c[k], j + u, LPR);
+          const int cs = __shfl_sync(gmask, c[k], j + u, LPR);
           s[u] = __shfl_sync(gmask, v[k], j + u, LPR);
-          const float *brow = a.B + (int64_t)cj * a.ldb;
+          const uint64_t pol = col_policy(cs, pol_hot, pol_cold);
+          const float *brow = a.B + (int64_t)col_id(cs) * a.ldb;
 #pragma unroll
           for (int w = 0; w < VPL; ++w) {
             const int col = col0 + w * LPR * W;
@@ -277,7 +292,7 @@ __global__ void __launch_bounds__(kSpmmThreads) spmm_nnz_kernel(const SpmmArgs a
   const int col0 = blockIdx.y * (LPR * VPL * W) + lane * W;
   const int64_t s = chunk * a.chunk_nnz, e = min(s + a.chunk_nnz, a.nnz);
   const int32_t head_slot = a.chunk_slot[2 * chunk], tail_slot = a.chunk_slot[2 * chunk + 1];
-  const uint64_t pol = evict_last_policy();
+  const uint64_t pol_hot = evict_last_policy(), pol_cold = evict_first_policy();
 
   int32_t row = a.coo_row[s];
   const int32_t head_row = row;
@@ -311,10 +326,11 @@ __global__ void __launch_bounds__(kSpmmThreads) spmm_nnz_kernel(const SpmmArgs a
         int ru[U];
 #pragma unroll
         for (int u = 0; u < U; ++u) {
-          const int cj = __shfl_sync(gmask, c[k], j + u, LPR);
+          const int cs = __shfl_sync(gmask, c[k], j + u, LPR);
           sv[u] = __shfl_sync(gmask, v[k], j + u, LPR);
           ru[u] = __shfl_sync(gmask, rr[k], j + u, LPR);
-          const float *brow = a.B + (int64_t)cj * a.ldb;
+          const uint64_t pol = col_policy(cs, pol_hot, pol_cold);
+          const float *brow = a.B + (int64_t)col_id(cs) * a.ldb;
 #pragma unroll
           for (int w = 0; w < VPL; ++w) {
             const int col = col0 + w * LPR * W;
@@ -365,7 +381,7 @@ __global__ void __launch_bounds__(kSpmmThreads, kMinBlocks) spmm_warp_kernel(con
   const int col0 = blockIdx.y * (128 * VPL) + lane * 4;
   const int64_t s = chunk * a.chunk_nnz, e = min(s + a.chunk_nnz, a.nnz);
   const int32_t head_slot = a.chunk_slot[2 * chunk], tail_slot = a.chunk_slot[2 * chunk + 1];
-  const uint64_t pol = evict_last_policy();
+  const uint64_t pol_hot = evict_last_policy(), pol_cold = evict_first_policy();
 
   int32_t row = __ldg(a.coo_row + s);
   const int32_t head_row = row;
@@ -404,10 +420,11 @@ __global__ void __launch_bounds__(kSpmmThreads, kMinBlocks) spmm_warp_kernel(con
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const bool ok = p + u < e;
-      const int32_t c = ok ? __ldg(a.cols + p + u) : 0;
+      const int32_t cs = ok ? __ldg(a.cols + p + u) : 0;
       v[u] = ok ? __ldg(a.vals + p + u) : 0.f;
       r[u] = ok ? __ldg(a.coo_row + p + u) : row;
-      const float *brow = a.B + (int64_t)c * a.ldb + col0;
+      const uint64_t pol = col_policy(cs, pol_hot, pol_cold);
+      const float *brow = a.B + (int64_t)col_id(cs) * a.ldb + col0;
 #pragma unroll
       for (int w = 0; w < VPL; ++w) b[u][w] = ok ? V::ldg(brow + 128 * w, pol) : V::zero();
     }
@@ -893,6 +910,51 @@ static bool dia_form(int64_t m, const int32_t *row_ids, const int64_t *rp, const
   return true;
 }
 
+// Bit 31 of the stored column ids (see col_policy): set on the columns whose B rows should
+// stay in L2. When the distinct columns' rows fit in half of the L2 (or DSP_SPMM_HOT=0),
+// every column is hot and all B rows are read with evict_last. Otherwise the most-referenced
+// columns whose rows fill half of the L2 are hot and the rest are read with evict_first:
+// on a power-law matrix whose B is many times the L2 (R-MAT scale 24: 8.6 GB of B, the top
+// 246 K columns, 120 MB, carry 67 % of the nonzeros) the hot rows then survive the stream
+// of rows used once. Returns the number of hot columns.
+static int64_t mark_hot_columns(int device, int64_t cols, int dims, int64_t nnz, int32_t *c32) {
+  static const int env_hot = [] {
+    const char *e = getenv("DSP_SPMM_HOT");
+    return e ? atoi(e) : 1;
+  }();
+  int l2 = 0;
+  if (cudaDeviceGetAttribute(&l2, cudaDevAttrL2CacheSize, device) != cudaSuccess || l2 <= 0) {
+    cudaGetLastError();
+    l2 = 126 << 20;
+  }
+  const int64_t budget = std::max<int64_t>(1, (int64_t)l2 / 2 / ((int64_t)std::max(dims, 1) * 4));
+  auto mark_all = [&]() {
+    parallel_for(nnz, [&](int64_t b, int64_t e) {
+      for (int64_t j = b; j < e; ++j) c32[j] |= INT32_MIN;
+    }, 1 << 16);
+    return cols;
+  };
+  if (!env_hot || nnz == 0 || cols <= budget) return mark_all();
+  std::vector<uint32_t> cnt((size_t)cols, 0);
+  parallel_for(nnz, [&](int64_t b, int64_t e) {
+    for (int64_t j = b; j < e; ++j) __atomic_fetch_add(&cnt[(size_t)c32[j]], 1u, __ATOMIC_RELAXED);
+  }, 1 << 16);
+  int64_t distinct = 0;
+  for (uint32_t x : cnt) distinct += x > 0;
+  if (distinct <= budget) return mark_all();
+  // the count of the budget-th most-referenced column; columns above it are hot
+  std::vector<uint32_t> sorted(cnt);
+  std::nth_element(sorted.begin(), sorted.begin() + (budget - 1), sorted.end(), std::greater<uint32_t>());
+  const uint32_t thr = sorted[(size_t)(budget - 1)];
+  int64_t hot = 0;
+  for (uint32_t x : cnt) hot += x > thr;
+  parallel_for(nnz, [&](int64_t b, int64_t e) {
+    for (int64_t j = b; j < e; ++j)
+      if (cnt[(size_t)c32[j]] > thr) c32[j] |= INT32_MIN;
+  }, 1 << 16);
+  return hot;
+}
+
 int DevOperand::upload(int device_, int64_t rows_, int64_t cols_, const int64_t *row_ptr, const int32_t *row_ids,
                        int64_t m, const int64_t *indices, const float *values, int64_t first_nz, int64_t nnz_,
                        int dims, bool include_empty, int variant_) {
@@ -955,6 +1017,7 @@ int DevOperand::upload(int device_, int64_t rows_, int64_t cols_, const int64_t 
       v32[(size_t)j] = values[first_nz + j];
     }
   }, 1 << 16);
+  hot_cols = mark_hot_columns(device_, cols_, dims, nnz, c32.data());
   if ((rc = dev_upload(&d_split_row, split_row.data(), sizeof(int32_t) * split_row.size())) ||
       (rc = dev_upload(&d_split_ptr, split_ptr.data(), sizeof(int32_t) * split_ptr.size())) ||
       (rc = dev_upload(&d_cols, c32.data(), sizeof(int32_t) * (size_t)padded)) ||
