@@ -55,7 +55,9 @@ struct SpmmArgs {
   int64_t dia_m;            // listed rows (consecutive output rows from dia_row0)
   int64_t dia_row0;
   int n_diag;
-  int32_t diag_off[kMaxDiag];  // ascending
+  int32_t diag_off[kMaxDiag];   // ascending
+  int n_runs;                    // runs of consecutive offsets (o, o+1, ..., at most 4 long)
+  uint8_t run_len[kMaxDiag];     // in offset order
 };
 
 struct SpmmShape {
@@ -107,6 +109,8 @@ struct DevOperand {
   int64_t dia_row0 = 0;
   int n_diag = 0;
   int32_t diag_off[kMaxDiag] = {};
+  int n_runs = 0;
+  uint8_t run_len[kMaxDiag] = {};
 
   // Rows i < m with nonzeros [row_ptr[i], row_ptr[i+1]) of indices/values (offsets are
   // absolute; first_nz is subtracted); row_ids[i] is the output row (nullptr = i).

@@ -361,6 +361,19 @@ __global__ void __launch_bounds__(kSpmmThreads) spmm_nnz_kernel(const SpmmArgs a
 
 // ------------------------------------------------------------------ nnz-split, warp per chunk
 
+// 4 consecutive 32-bit words read by every lane of the warp from the same 16-byte address
+// (one request, served to the whole warp).
+__device__ __forceinline__ int4 ldg_uniform_i4(const int32_t *p) {
+  int4 v;
+  asm("ld.global.nc.v4.s32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ float4 ldg_uniform_f4(const float *p) {
+  float4 v;
+  asm("ld.global.nc.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
+  return v;
+}
+
 // One chunk of chunk_nnz consecutive nonzeros per warp; lane l holds output columns
 // col0 + 128 v .. +3 (v < VPL) of the current row, blockIdx.y selecting a block of
 // 128 * VPL columns. Each step reads the column, value and output row of U nonzeros (every
@@ -374,6 +387,7 @@ __global__ void __launch_bounds__(kSpmmThreads) spmm_nnz_kernel(const SpmmArgs a
 // 1.43 ms on the R-MAT scale-20 stream).
 template <int VPL, int U, bool kAccum, int kMinBlocks>
 __global__ void __launch_bounds__(kSpmmThreads, kMinBlocks) spmm_warp_kernel(const SpmmArgs a) {
+  static_assert(U % 4 == 0, "steps read groups of 4 nonzeros");
   using V = Vec<4>;
   const int lane = threadIdx.x & 31;
   const int64_t chunk = ((int64_t)blockIdx.x * kSpmmThreads + threadIdx.x) >> 5;
@@ -412,35 +426,54 @@ __global__ void __launch_bounds__(kSpmmThreads, kMinBlocks) spmm_warp_kernel(con
   if (!kAccum && a.zero_rows > 0) zeros(s > 0 ? (int64_t)__ldg(a.coo_row + s - 1) + 1 : 0, row);
 #pragma unroll
   for (int w = 0; w < VPL; ++w) acc[w] = V::zero();
+  // nonzero with column cs, value v, row r (warp-uniform row change)
+  auto add = [&](int32_t r, float v, const float4 (&b)[VPL]) {
+    if (r != row) {
+      flush(row == head_row ? head_slot : -1);
+      if (!kAccum && a.zero_rows > 0) zeros((int64_t)row + 1, r);
+      row = r;
+#pragma unroll
+      for (int w = 0; w < VPL; ++w) acc[w] = V::zero();
+    }
+#pragma unroll
+    for (int w = 0; w < VPL; ++w) V::fma(acc[w], v, b[w]);
+  };
 
-  for (int64_t p = s; p < e; p += U) {
-    float4 b[U][VPL];
+  // full steps of U nonzeros: p stays a multiple of 4 (chunk_nnz is a multiple of 16), so
+  // the column ids, values and row ids of 4 nonzeros come in one 16-byte load each, and no
+  // entry needs a bounds test
+  int64_t p = s;
+  for (; p + U <= e; p += U) {
+    int32_t cs[U], r[U];
     float v[U];
-    int32_t r[U];
+#pragma unroll
+    for (int q = 0; q < U / 4; ++q) {
+      const int4 c4 = ldg_uniform_i4(a.cols + p + 4 * q);
+      const float4 v4 = ldg_uniform_f4(a.vals + p + 4 * q);
+      const int4 r4 = ldg_uniform_i4(a.coo_row + p + 4 * q);
+      cs[4 * q] = c4.x, cs[4 * q + 1] = c4.y, cs[4 * q + 2] = c4.z, cs[4 * q + 3] = c4.w;
+      v[4 * q] = v4.x, v[4 * q + 1] = v4.y, v[4 * q + 2] = v4.z, v[4 * q + 3] = v4.w;
+      r[4 * q] = r4.x, r[4 * q + 1] = r4.y, r[4 * q + 2] = r4.z, r[4 * q + 3] = r4.w;
+    }
+    float4 b[U][VPL];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const bool ok = p + u < e;
-      const int32_t cs = ok ? __ldg(a.cols + p + u) : 0;
-      v[u] = ok ? __ldg(a.vals + p + u) : 0.f;
-      r[u] = ok ? __ldg(a.coo_row + p + u) : row;
-      const uint64_t pol = col_policy(cs, pol_hot, pol_cold);
-      const float *brow = a.B + (int64_t)col_id(cs) * a.ldb + col0;
+      const float *brow = a.B + (int64_t)col_id(cs[u]) * a.ldb + col0;
+      const uint64_t pol = col_policy(cs[u], pol_hot, pol_cold);
 #pragma unroll
-      for (int w = 0; w < VPL; ++w) b[u][w] = ok ? V::ldg(brow + 128 * w, pol) : V::zero();
+      for (int w = 0; w < VPL; ++w) b[u][w] = V::ldg(brow + 128 * w, pol);
     }
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      if (p + u >= e) break;  // past the chunk's end (its last step)
-      if (r[u] != row) {      // warp-uniform: the chunk crosses into the next row
-        flush(row == head_row ? head_slot : -1);
-        if (!kAccum && a.zero_rows > 0) zeros((int64_t)row + 1, r[u]);
-        row = r[u];
+    for (int u = 0; u < U; ++u) add(r[u], v[u], b[u]);
+  }
+  // the chunk's last nonzeros (the matrix's end)
+  for (; p < e; ++p) {
+    const int32_t cs = __ldg(a.cols + p);
+    float4 b[VPL];
+    const float *brow = a.B + (int64_t)col_id(cs) * a.ldb + col0;
 #pragma unroll
-        for (int w = 0; w < VPL; ++w) acc[w] = V::zero();
-      }
-#pragma unroll
-      for (int w = 0; w < VPL; ++w) V::fma(acc[w], v[u], b[u][w]);
-    }
+    for (int w = 0; w < VPL; ++w) b[w] = V::ldg(brow + 128 * w, col_policy(cs, pol_hot, pol_cold));
+    add(__ldg(a.coo_row + p), __ldg(a.vals + p), b);
   }
   flush(tail_slot >= 0 ? tail_slot : (row == head_row ? head_slot : -1));
   if (!kAccum && a.zero_rows > 0 && chunk == a.n_chunks - 1) zeros((int64_t)row + 1, a.zero_rows);
@@ -453,59 +486,85 @@ __global__ void __launch_bounds__(kSpmmThreads, kMinBlocks) spmm_warp_kernel(con
 // up to 4, e.g. the x-neighbours of a stencil) share B rows: the 8 rows of a block need
 // B rows jb + k, k < 8 + L - 1, of a run of length L, and each such row is read once and
 // applied to every row r = k - l of the block it touches, so a 27-point stencil reads about
-// 11 B rows per output row instead of 27, and no column ids. Presence bits (one byte per
-// block and diagonal) mark the entries that exist: a B row no entry of the block uses is
-// not read and an absent entry adds nothing, so the result is the CSR product exactly (an
-// explicit zero in A counts as present). Lane l holds output columns col0 .. col0 + 3,
-// blockIdx.y selecting a block of 128 columns. Needs N % 128 == 0 and 16-byte aligned B / C
-// rows.
+// 11 B rows per output row instead of 27, and no column ids. The block's values are staged
+// once in shared memory (one load latency per block, then broadcast reads); each run is
+// done by code specialised for its length (run_len, set on the host). Presence bits (one
+// byte per block and diagonal) mark the entries that exist: a B row no entry of the block
+// uses is not read and an absent entry adds nothing, so the result is the CSR product
+// exactly (an explicit zero in A counts as present). Lane l holds output columns
+// col0 .. col0 + 3, blockIdx.y selecting a block of 128 columns. Needs N % 128 == 0 and
+// 16-byte aligned B / C rows.
+template <int L>
+__device__ __forceinline__ void dia_run(const SpmmArgs &a, const float *sv, int d0, const uint32_t (&pb)[4],
+                                        int64_t jb, int col0, uint64_t pol, float4 (&acc)[kDiaRows]) {
+  constexpr int R = kDiaRows;
+  using V = Vec<4>;
+  bool all = true;  // every entry of the run is present: no per-entry tests
+#pragma unroll
+  for (int l = 0; l < L; ++l) all = all && pb[l] == 0xffu;
+  float4 b[R + L - 1];
+#pragma unroll
+  for (int k = 0; k < R + L - 1; ++k) {
+    uint32_t need = all ? 1u : 0u;  // some present entry of the block uses B row jb + k
+#pragma unroll
+    for (int l = 0; l < L; ++l)
+      if (k - l >= 0 && k - l < R) need |= (pb[l] >> (k - l)) & 1u;
+    b[k] = need ? V::ldg(a.B + (jb + k) * a.ldb + col0, pol) : V::zero();
+  }
+  if (all) {
+#pragma unroll
+    for (int k = 0; k < R + L - 1; ++k)
+#pragma unroll
+      for (int l = 0; l < L; ++l)
+        if (k - l >= 0 && k - l < R) V::fma(acc[k - l], sv[(d0 + l) * R + k - l], b[k]);
+  } else {
+#pragma unroll
+    for (int k = 0; k < R + L - 1; ++k)
+#pragma unroll
+      for (int l = 0; l < L; ++l)
+        if (k - l >= 0 && k - l < R && ((pb[l] >> (k - l)) & 1u)) V::fma(acc[k - l], sv[(d0 + l) * R + k - l], b[k]);
+  }
+}
+
 template <bool kAccum>
 __global__ void __launch_bounds__(kSpmmThreads) spmm_dia_kernel(const SpmmArgs a) {
   constexpr int R = kDiaRows;
   using V = Vec<4>;
+  __shared__ float s_val[kSpmmThreads / 32][kMaxDiag * R];
   const unsigned full = 0xffffffffu;
-  const int lane = threadIdx.x & 31;
+  const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
   const int64_t blk = ((int64_t)blockIdx.x * kSpmmThreads + threadIdx.x) >> 5;
   const int64_t i0 = blk * R;
   if (i0 >= a.dia_m) return;
   const int col0 = blockIdx.y * 128 + lane * 4;
   const int64_t orow0 = a.dia_row0 + i0;
   const uint64_t pol = evict_last_policy();
+  // the block's values, diagonal-major (8 rows each), into this warp's shared slice
+  float *sv = s_val[wib];
+  for (int idx = lane; idx < a.n_diag * R; idx += 32) {
+    const int d = idx / R, r = idx % R;
+    sv[idx] = i0 + r < a.dia_m ? __ldg(a.dia_vals + (int64_t)d * a.dia_m + i0 + r) : 0.f;
+  }
   // lane d holds the presence bits of diagonal d for the 8 rows of this block
   const uint32_t pbyte = lane < a.n_diag ? __ldg(a.dia_pres + blk * a.n_diag + lane) : 0u;
+  __syncwarp();
   float4 acc[R];
 #pragma unroll
   for (int r = 0; r < R; ++r) acc[r] = V::zero();
 
-  for (int d0 = 0; d0 < a.n_diag;) {
-    int L = 1;  // run of consecutive offsets from d0 (warp-uniform)
-    while (d0 + L < a.n_diag && L < 4 && a.diag_off[d0 + L] == a.diag_off[d0] + L) ++L;
-    // lane t = l * 8 + r holds the value of (row i0 + r, diagonal d0 + l)
-    const int tl = lane / R, tr = lane % R;
-    const uint32_t pb = __shfl_sync(full, pbyte, min(d0 + tl, 31));
-    const bool pres = tl < L && ((pb >> tr) & 1u);
-    const float myv = pres ? __ldg(a.dia_vals + (int64_t)(d0 + tl) * a.dia_m + i0 + tr) : 0.f;
-    const uint32_t pm = __ballot_sync(full, pres);
+  int d0 = 0;
+  for (int q = 0; q < a.n_runs; ++q) {
+    const int L = a.run_len[q];
+    uint32_t pb[4];
+#pragma unroll
+    for (int l = 0; l < 4; ++l) pb[l] = __shfl_sync(full, pbyte, min(d0 + l, 31));
     const int64_t jb = orow0 + a.diag_off[d0];  // B row of k = 0
-    float4 b[R + 3];
-#pragma unroll
-    for (int k = 0; k < R + 3; ++k) {
-      uint32_t need = 0;  // some present entry of the block uses B row jb + k
-#pragma unroll
-      for (int l = 0; l < 4; ++l)
-        if (k - l >= 0 && k - l < R) need |= (pm >> (l * R + k - l)) & 1u;
-      b[k] = need ? V::ldg(a.B + (jb + k) * a.ldb + col0, pol) : V::zero();
+    switch (L) {
+      case 1: dia_run<1>(a, sv, d0, pb, jb, col0, pol, acc); break;
+      case 2: dia_run<2>(a, sv, d0, pb, jb, col0, pol, acc); break;
+      case 3: dia_run<3>(a, sv, d0, pb, jb, col0, pol, acc); break;
+      default: dia_run<4>(a, sv, d0, pb, jb, col0, pol, acc); break;
     }
-#pragma unroll
-    for (int k = 0; k < R + 3; ++k)
-#pragma unroll
-      for (int l = 0; l < 4; ++l) {
-        const int r = k - l;
-        if (r >= 0 && r < R) {
-          const float v = __shfl_sync(full, myv, l * R + r);
-          if ((pm >> (l * R + r)) & 1u) V::fma(acc[r], v, b[k]);
-        }
-      }
     d0 += L;
   }
 #pragma unroll
@@ -628,7 +687,7 @@ bool aligned(const void *p, uintptr_t bytes) { return ((uintptr_t)p & (bytes - 1
 
 // Warp-per-chunk shapes: vectors of 4 floats per lane per 128 columns, nonzeros per step,
 // and the blocks per SM the register allocation is held to (1: the compiler's choice).
-#define DSP_WARP_SHAPES(X) X(1, 2, 1) X(1, 4, 1) X(1, 4, 5) X(1, 8, 1) X(2, 2, 1) X(2, 4, 1) X(4, 2, 1)
+#define DSP_WARP_SHAPES(X) X(1, 4, 1) X(1, 4, 5) X(1, 8, 1) X(2, 4, 1) X(4, 4, 1)
 
 KernelFn warp_kernel_for(int VPL, int U, bool accum, int MB = 1) {
 #define DSP_WK(P, Q, B) \
@@ -667,7 +726,7 @@ WarpShape warp_shape(int N, const float *B, int64_t ldb, const float *C, int64_t
   const int n128 = N / 128;
   int vpl = n128 % 4 == 0 ? 4 : n128 % 2 == 0 ? 2 : 1;
   if (env_vpl > 0 && n128 % env_vpl == 0) vpl = env_vpl;
-  int u = vpl == 4 ? 2 : 4;
+  int u = 4;
   if (env_u > 0) u = env_u;
   const int mb = warp_kernel_for(vpl, u, false, env_mb) ? env_mb : 1;
   if (!warp_kernel_for(vpl, u, false, mb)) return w;
@@ -745,7 +804,8 @@ int launch_spmm(const SpmmArgs &a, bool accumulate, cudaStream_t stream) {
   const SpmmShape s = spmm_shape(a.N, a.variant, a.B, a.ldb, a.C, a.ldc);
   if (s.chunks > 65535) return fail(DSP_ERR_UNSUPPORTED, "spmm: N = %d too wide", a.N);
   const int64_t units = a.variant == kRowSplit ? a.n_items : a.n_chunks;
-  const WarpShape ws = a.variant == kNnzSplit ? warp_shape(a.N, a.B, a.ldb, a.C, a.ldc) : WarpShape();
+  const WarpShape ws = a.variant == kNnzSplit && a.chunk_nnz % 16 == 0 ? warp_shape(a.N, a.B, a.ldb, a.C, a.ldc)
+                                                                       : WarpShape();
   // banded row-split operands: the diagonal kernel (DSP_SPMM_DIA=0 turns it off)
   static const int env_dia = [] {
     const char *e = getenv("DSP_SPMM_DIA");
@@ -840,7 +900,7 @@ int64_t wave_chunk_nnz(int device, int dims, int64_t nnz) {
   const int64_t resident = (int64_t)sms * per_sm * (kSpmmThreads / lanes) / std::max(col_blocks, 1);
   const int64_t waves = std::max<int64_t>(2, (nnz + c * resident - 1) / (c * resident));
   const int64_t len = std::max<int64_t>(8, (nnz + waves * resident - 1) / (waves * resident));
-  return len;
+  return (len + 15) / 16 * 16;  // the warp-per-chunk kernel reads 4-nonzero groups at 16-byte addresses
 }
 
 // The diagonal form of listed rows [0, m) when they are consecutive output rows
@@ -976,7 +1036,14 @@ int DevOperand::upload(int device_, int64_t rows_, int64_t cols_, const int64_t 
   zero_rows = include_empty ? rows_ : 0;
   std::vector<int64_t> rp((size_t)m + 1);
   for (int64_t i = 0; i <= m; ++i) rp[(size_t)i] = row_ptr[i] - first_nz;
-  variant = variant_ >= 0 ? variant_ : choose_variant(m, rp.data(), dims);
+  // a banded operand runs on the diagonal kernel (with the row-split items as its fallback
+  // for widths that kernel does not take), whatever its row lengths
+  std::vector<int32_t> offs;
+  std::vector<float> dv;
+  std::vector<uint8_t> pres;
+  const bool banded = variant_ != kNnzSplit &&
+                      dia_form(m, row_ids, rp.data(), indices + first_nz, values + first_nz, &dia_row0, &offs, &dv, &pres);
+  variant = variant_ >= 0 ? variant_ : banded ? (int)kRowSplit : choose_variant(m, rp.data(), dims);
   std::vector<int32_t> split_row, split_ptr;
   int rc;
   if (variant == kRowSplit) {
@@ -991,12 +1058,16 @@ int DevOperand::upload(int device_, int64_t rows_, int64_t cols_, const int64_t 
     if ((rc = dev_upload(&d_item_ptr, plan.item_ptr.data(), sizeof(int64_t) * plan.item_ptr.size())) ||
         (rc = dev_upload(&d_item_out, plan.item_out.data(), sizeof(int32_t) * plan.item_out.size())))
       return rc;
-    std::vector<int32_t> offs;
-    std::vector<float> dv;
-    std::vector<uint8_t> pres;
-    if (dia_form(m, row_ids, rp.data(), indices + first_nz, values + first_nz, &dia_row0, &offs, &dv, &pres)) {
+    if (banded) {
       n_diag = (int)offs.size();
       for (int d = 0; d < n_diag; ++d) diag_off[d] = offs[(size_t)d];
+      n_runs = 0;
+      for (int d = 0; d < n_diag;) {  // runs of consecutive offsets, at most 4 long
+        int len = 1;
+        while (d + len < n_diag && len < 4 && offs[(size_t)(d + len)] == offs[(size_t)d] + len) ++len;
+        run_len[n_runs++] = (uint8_t)len;
+        d += len;
+      }
       n_lrows = m;
       if ((rc = dev_upload(&d_dia_vals, dv.data(), sizeof(float) * dv.size())) ||
           (rc = dev_upload(&d_dia_pres, pres.data(), pres.size())))
@@ -1044,7 +1115,7 @@ void DevOperand::release() {
     *p = nullptr;
   }
   n_items = n_chunks = n_split = pieces = n_lrows = 0;
-  n_diag = 0;
+  n_diag = n_runs = 0;
 }
 
 int64_t DevOperand::device_bytes() const {
@@ -1068,6 +1139,8 @@ SpmmArgs DevOperand::args(const float *B, int64_t ldb, float *C, int64_t ldc, in
   a.dia_row0 = dia_row0;
   a.n_diag = n_diag;
   memcpy(a.diag_off, diag_off, sizeof diag_off);
+  a.n_runs = n_runs;
+  memcpy(a.run_len, run_len, sizeof run_len);
   a.n_chunks = n_chunks;
   a.chunk_nnz = chunk_nnz;
   a.nnz = nnz;
