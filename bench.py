@@ -677,7 +677,7 @@ def main(argv=None):
         "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config_of(a, world, nnz, M),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic,
-                     "kernel": "spmm_nnz_kernel / spmm_rows_kernel (+fixup, zero rows)", "rank": rank,
+                     "kernel": "the rank's SpMM phases: spmm_warp_kernel (nnz-split) / spmm_dia_kernel (banded) / spmm_rows_kernel, + fixup and zero rows", "rank": rank,
                      "alg_bytes_per_launch": alg_bytes, "launch_ms": round(mean_compute, 4),
                      "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})"},
         "e2e": e2e, "cpu_baseline": cpu, "cusparse": cus, "check": check, "clocks": clk,

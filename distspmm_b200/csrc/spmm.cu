@@ -687,7 +687,7 @@ bool aligned(const void *p, uintptr_t bytes) { return ((uintptr_t)p & (bytes - 1
 
 // Warp-per-chunk shapes: vectors of 4 floats per lane per 128 columns, nonzeros per step,
 // and the blocks per SM the register allocation is held to (1: the compiler's choice).
-#define DSP_WARP_SHAPES(X) X(1, 4, 1) X(1, 4, 5) X(1, 8, 1) X(2, 4, 1) X(4, 4, 1)
+#define DSP_WARP_SHAPES(X) X(1, 4, 1) X(1, 4, 5) X(1, 8, 1) X(2, 4, 1) X(2, 4, 3) X(4, 4, 1)
 
 KernelFn warp_kernel_for(int VPL, int U, bool accum, int MB = 1) {
 #define DSP_WK(P, Q, B) \
@@ -718,17 +718,20 @@ WarpShape warp_shape(int N, const float *B, int64_t ldb, const float *C, int64_t
   }();
   static const int env_mb = [] {
     const char *e = getenv("DSP_SPMM_WARP_MB");
-    return e ? atoi(e) : 1;
+    return e ? atoi(e) : 0;
   }();
   WarpShape w;
   if (!env_on || N <= 0 || N % 128 != 0 || ldb % 4 != 0 || ldc % 4 != 0 || !aligned(B, 16) || !aligned(C, 16))
     return w;
+  // One float4 per lane (128 columns per launch row of blocks, blockIdx.y covering wider B)
+  // and 4 nonzeros per step, with the registers held to 48 so that 5 blocks (40 warps) fit
+  // an SM: measured best on R-MAT (scale 20: 1.32 ms against 1.46 uncapped and 1.92 with 8
+  // nonzeros per step; scale 24: 26.9 against 29.4 ms).
   const int n128 = N / 128;
-  int vpl = n128 % 4 == 0 ? 4 : n128 % 2 == 0 ? 2 : 1;
-  if (env_vpl > 0 && n128 % env_vpl == 0) vpl = env_vpl;
-  int u = 4;
-  if (env_u > 0) u = env_u;
-  const int mb = warp_kernel_for(vpl, u, false, env_mb) ? env_mb : 1;
+  const int vpl = env_vpl > 0 && n128 % env_vpl == 0 ? env_vpl : 1;
+  const int u = env_u > 0 ? env_u : 4;
+  const int dflt_mb = vpl == 1 && u == 4 ? 5 : vpl == 2 && u == 4 ? 3 : 1;
+  const int mb = env_mb > 0 && warp_kernel_for(vpl, u, false, env_mb) ? env_mb : dflt_mb;
   if (!warp_kernel_for(vpl, u, false, mb)) return w;
   w.VPL = vpl;
   w.U = u;
