@@ -74,8 +74,10 @@ def parse_args(argv=None):
                     help="A rows per rank: the reference's equal-row split or work-balanced (nnz + rows)")
     ap.add_argument("--fetch-scope", choices=["node", "rank"], default="rank",
                     help="remote B rows fetched: the node union of all ranks' needs (reference) or this rank's own")
-    ap.add_argument("--pipeline", choices=["auto", "rows", "split"], default="auto",
-                    help="phases: whole rows after their last fetch, nonzeros per ring position, or per matrix")
+    ap.add_argument("--pipeline", choices=["auto", "rows", "split", "groups"], default="auto",
+                    help="phases: whole rows after their last fetch, nonzeros per ring position, row groups "
+                         "fetched group by group, or per matrix")
+    ap.add_argument("--groups", type=int, default=0, help="row groups of the groups pipeline (0 = 8)")
     ap.add_argument("--fetch-streams", type=int, default=4, help="concurrent fetch streams (nvlink_num_producers)")
     ap.add_argument("--platform", choices=["h100", "a800", "b200"], default="b200",
                     help="adaptive selector constants (comm_type 2); b200 = the NVLink 5 fit of comm_test")
@@ -139,7 +141,7 @@ def config_of(a, world, nnz, M):
             "rows": M, "nnz": nnz, "dims": a.dims, "n_rolls": a.n_rolls, "task_dist": a.task_dist,
             "comm_type": a.comm_type, "parallelism": f"row1d_p{world}", "seed": a.seed,
             "partition": a.partition if world > 1 else "single rank", "fetch_scope": a.fetch_scope,
-            "pipeline": a.pipeline, "fetch_streams": a.fetch_streams, "selector_platform": a.platform,
+            "pipeline": a.pipeline, "groups": a.groups or 8, "fetch_streams": a.fetch_streams, "selector_platform": a.platform,
             "l2": "flushed between steps (512 MiB write)" if not a.no_flush else "not flushed",
             "b": "U(-1,1) fp32 row-major"}
 
@@ -459,7 +461,7 @@ def main(argv=None):
 
     def new_rank():
         X = make_rank(local, rank, world, local_rank, a.dims, M, lb, tiling, plan, a.comm_type, a.platform,
-                      a.fetch_streams, fetch_scope=a.fetch_scope, pipeline=a.pipeline)
+                      a.fetch_streams, fetch_scope=a.fetch_scope, pipeline=a.pipeline, groups=a.groups)
         if comm is not None:
             connect_peers(comm, X)
         return X
@@ -668,7 +670,7 @@ def main(argv=None):
     if comm is not None:
         fetch_bytes = comm.allreduce_sum_i64(fetch_bytes)
         per_rank = [[int(x) for x in r] for r in comm.allgather_i32(np.array(mine, np.int64).clip(max=2**31 - 1))]
-    ranks = [{"nnz": r[0], "rows": r[1], "pipeline": ["", "rows", "split"][r[2]], "compute_ms": r[3] / 1e4,
+    ranks = [{"nnz": r[0], "rows": r[1], "pipeline": ["", "rows", "split", "groups"][r[2]], "compute_ms": r[3] / 1e4,
               "idle_ms": r[4] / 1e4, "fetched_kib": r[5]} for r in per_rank]
     traffic = profile_traffic(workload_name(a)) if world == 1 else None
     line = {
@@ -682,7 +684,7 @@ def main(argv=None):
                      "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})"},
         "e2e": e2e, "cpu_baseline": cpu, "cusparse": cus, "check": check, "clocks": clk,
         "gpu_launches": a.steps * st["kernels_per_step"],
-        "nvlink": {"fetched_bytes_per_step": fetch_bytes, "pipeline_rank0": ["", "rows", "split"][st["pipeline"]],
+        "nvlink": {"fetched_bytes_per_step": fetch_bytes, "pipeline_rank0": ["", "rows", "split", "groups"][st["pipeline"]],
                    "phase0_nnz_rank0": st["phase0_nnz"],
                    "max_rank_compute_ms": round(t_comp_max, 4),
                    "max_rank_compute_idle_ms": round(idle_max, 4),

@@ -55,14 +55,14 @@ class dsp_rank_desc(ctypes.Structure):
                 ("n_streams", c_int), ("cpt", c_i64), ("M", c_i64), ("m_lb", c_i64),
                 ("local", P(dsp_csr)), ("remap", P(c_i32)), ("sparse", P(ctypes.c_uint8)),
                 ("needed_offsets", P(c_i64)), ("needed_cols", P(c_i32)), ("n_slice", P(c_i32)),
-                ("fetch_engine", c_int), ("pipeline", c_int)]
+                ("fetch_engine", c_int), ("pipeline", c_int), ("groups", c_int)]
 
 
 class dsp_rank_stats(ctypes.Structure):
     _fields_ = [(n, c_i64) for n in ("m_local", "nnz_local", "segments", "fetch_rows", "fetch_bytes",
                                      "fetch_bulk_tiles", "fetch_sparse_tiles", "owned_rows",
                                      "distinct_cols", "launches_per_step", "kernels_per_step",
-                                     "device_bytes", "pipeline", "phase0_nnz")]
+                                     "device_bytes", "pipeline", "phase0_nnz", "timeline_len")]
 
 
 class dsp_args(ctypes.Structure):

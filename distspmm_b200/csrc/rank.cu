@@ -86,6 +86,12 @@ struct dsp_rank {
     int64_t n_rows = 0;
   };
   std::vector<Fetch> fetch;  // by segment index k (k = 0 unused)
+  // groups pipeline: segs[g] holds row group g; gfetch[g * P + k] the rows of peer (me+k)%P
+  // that group g is the first to need; bulk tiles (fetch[k].bulk) land before group 0
+  int n_groups = 0;
+  std::vector<int64_t> group_end;  // first local row after group g
+  std::vector<Fetch> gfetch;
+  std::vector<cudaEvent_t> ev_group;  // [g * P + k]
 
   std::vector<const float *> peer_B;
   std::vector<int> peer_dev;
@@ -153,7 +159,9 @@ int build_split_phases(dsp_rank *r, const dsp_csr *a, const std::vector<int32_t>
 // computed once, with all its nonzeros, after the fetches of ring positions 1..k. The
 // split pipeline (chosen here for DSP_PIPELINE_AUTO when less than half of the nonzeros
 // would run before any fetch lands) cuts rows by ring position instead.
-int build_phases(dsp_rank *r, const dsp_csr *a, int pipeline) {
+int build_groups(dsp_rank *r, const dsp_csr *a, int groups);
+
+int build_phases(dsp_rank *r, const dsp_csr *a, int pipeline, int groups) {
   const int P = r->P, me = r->me;
   const int64_t m = a->num_rows, cpt = r->cpt;
   std::vector<int32_t> phase((size_t)std::max<int64_t>(m, 1), -1), first((size_t)std::max<int64_t>(m, 1), -1);
@@ -204,12 +212,16 @@ int build_phases(dsp_rank *r, const dsp_csr *a, int pipeline) {
   // local but 8.7 per accumulated piece) and P = 4 (8.4) slower split; the stencil is
   // rows-bound.
   if (pipeline == DSP_PIPELINE_AUTO)
-    pipeline = 2 * rows_phase0_nnz < a->nnz && 10 * local_nnz >= 3 * a->nnz && acc_pieces > 0 &&
-                       acc_nnz >= 12 * acc_pieces
+    pipeline = 2 * rows_phase0_nnz >= a->nnz ? DSP_PIPELINE_ROWS
+               : 10 * local_nnz >= 3 * a->nnz && acc_pieces > 0 && acc_nnz >= 12 * acc_pieces
                    ? DSP_PIPELINE_SPLIT
-                   : DSP_PIPELINE_ROWS;
+                   : DSP_PIPELINE_GROUPS;
   if (P == 1 || P > 64) pipeline = DSP_PIPELINE_ROWS;
   r->pipeline = pipeline;
+  if (pipeline == DSP_PIPELINE_GROUPS) {
+    r->stats.phase0_nnz = 0;
+    return build_groups(r, a, groups);
+  }
   if (pipeline == DSP_PIPELINE_SPLIT) {
     r->stats.phase0_nnz = local_nnz;
     return build_split_phases(r, a, first);
@@ -280,6 +292,100 @@ int build_fetch(dsp_rank *r, const dsp_rank_desc *d) {
   return DSP_OK;
 }
 
+// Groups pipeline: the local rows in G contiguous groups of equal cost (nonzeros + rows),
+// one operand each (its rows listed with their own ids, so banded groups keep the diagonal
+// form); rows without nonzeros are zero-filled apart, as in the other pipelines.
+int build_groups(dsp_rank *r, const dsp_csr *a, int groups) {
+  const int64_t m = a->num_rows;
+  const int G = (int)std::max<int64_t>(1, std::min<int64_t>(groups > 0 ? groups : 8, std::max<int64_t>(m, 1)));
+  r->n_groups = G;
+  r->segs.assign((size_t)G, dsp_rank::Segment());
+  r->group_end.assign((size_t)G, m);
+  const int64_t total = a->nnz + m;
+  int64_t rb = 0;
+  std::vector<int32_t> ids;
+  for (int g = 0; g < G; ++g) {
+    // first row of group g + 1: cost(indptr[i] + i) reaches (g + 1) / G of the total
+    const int64_t target = (total * (g + 1) + G - 1) / G;
+    int64_t lo = rb, hi = m;
+    while (lo < hi) {
+      const int64_t mid = (lo + hi) / 2;
+      if (a->indptr[mid] + mid >= target) hi = mid;
+      else lo = mid + 1;
+    }
+    const int64_t re = g == G - 1 ? m : lo;
+    auto &S = r->segs[(size_t)g];
+    S.owner = -1;
+    const int64_t nz = a->indptr[re] - a->indptr[rb];
+    if (re > rb && nz > 0) {
+      ids.resize((size_t)(re - rb));
+      for (int64_t i = rb; i < re; ++i) ids[(size_t)(i - rb)] = (int32_t)i;
+      int rc = S.op.upload(r->device, m, r->M, a->indptr + rb, ids.data(), re - rb, a->indices, a->values,
+                           a->indptr[rb], nz, r->dims, false);
+      if (rc) return rc;
+      r->scratch_floats = std::max(r->scratch_floats, S.op.pieces * (int64_t)r->dims);
+    }
+    r->group_end[(size_t)g] = re;
+    rb = re;
+  }
+  return DSP_OK;
+}
+
+// Groups pipeline fetch plan: every remote row of a sparse tile is fetched with the first
+// group whose nonzeros use it, in ascending row order per (group, peer); bulk tiles with
+// local nonzeros are copied whole before group 0 (tiles without local nonzeros are
+// skipped, src/dist_spmm_node.cu:344).
+int build_group_fetch(dsp_rank *r, const dsp_rank_desc *d) {
+  const int P = r->P, T = r->T, G = r->n_groups, me = r->me;
+  const dsp_csr *a = d->local;
+  std::vector<int64_t> nnz_t((size_t)T, 0);
+  for (int64_t j = 0; j < a->nnz; ++j) nnz_t[(size_t)(a->indices[j] / r->cpt)]++;
+  r->fetch.assign((size_t)P, dsp_rank::Fetch());
+  for (int t = 0; t < T; ++t) {
+    const int q = r->remap[(size_t)t];
+    if (q == me || nnz_t[(size_t)t] == 0) continue;
+    if (r->sparse[(size_t)t]) {
+      r->stats.fetch_sparse_tiles++;
+    } else {
+      const int64_t row0 = (int64_t)t * r->cpt, n = std::min<int64_t>(r->cpt, r->M - row0);
+      if (n > 0) r->fetch[(size_t)((q - me + P) % P)].bulk.push_back({row0, n});
+      r->stats.fetch_bulk_tiles++;
+      r->stats.fetch_rows += n;
+    }
+  }
+  // first group needing each remote row of a sparse tile (groups are contiguous row ranges)
+  std::vector<uint8_t> first((size_t)r->M, 0xff);
+  int g = 0;
+  for (int64_t i = 0; i < a->num_rows; ++i) {
+    while (g + 1 < G && i >= r->group_end[(size_t)g]) ++g;
+    for (int64_t j = a->indptr[i]; j < a->indptr[i + 1]; ++j) {
+      const int64_t c = a->indices[j];
+      const int64_t t = c / r->cpt;
+      if (r->remap[(size_t)t] == me || !r->sparse[(size_t)t] || first[(size_t)c] != 0xff) continue;
+      first[(size_t)c] = (uint8_t)g;
+    }
+  }
+  std::vector<std::vector<int32_t>> lists((size_t)G * P);
+  for (int64_t c = 0; c < r->M; ++c) {
+    const uint8_t g = first[(size_t)c];
+    if (g == 0xff) continue;
+    const int q = r->remap[(size_t)(c / r->cpt)];
+    lists[(size_t)g * P + (size_t)((q - me + P) % P)].push_back((int32_t)c);
+  }
+  r->gfetch.assign((size_t)G * P, dsp_rank::Fetch());
+  for (size_t i = 0; i < lists.size(); ++i) {
+    auto &F = r->gfetch[i];
+    F.n_rows = (int64_t)lists[i].size();
+    r->stats.fetch_rows += F.n_rows;
+    if (F.n_rows) {
+      int rc = dev_upload(&F.d_rows, lists[i].data(), sizeof(int32_t) * lists[i].size());
+      if (rc) return rc;
+    }
+  }
+  r->stats.fetch_bytes = r->stats.fetch_rows * (int64_t)r->dims * 4;
+  return DSP_OK;
+}
+
 }  // namespace
 
 extern "C" int dsp_rank_create(const dsp_rank_desc *d, dsp_rank **out) {
@@ -334,8 +440,8 @@ extern "C" int dsp_rank_create(const dsp_rank_desc *d, dsp_rank **out) {
     return bail(fail(DSP_ERR_NOMEM, "C (%zu bytes): %s", cbytes, cudaGetErrorString(e)));
   if ((e = cudaMalloc(&r->d_err, sizeof(int))) != cudaSuccess || (e = cudaMemset(r->d_err, 0, sizeof(int))) != cudaSuccess)
     return bail(fail(DSP_ERR_NOMEM, "error flag: %s", cudaGetErrorString(e)));
-  if ((rc = build_phases(r, d->local, d->pipeline))) return bail(rc);
-  if (r->P > 1 && (rc = build_fetch(r, d))) return bail(rc);
+  if ((rc = build_phases(r, d->local, d->pipeline, d->groups))) return bail(rc);
+  if (r->P > 1 && (rc = r->n_groups > 0 ? build_group_fetch(r, d) : build_fetch(r, d))) return bail(rc);
   if (r->scratch_floats > 0 && (e = cudaMalloc(&r->scratch, sizeof(float) * (size_t)r->scratch_floats)) != cudaSuccess)
     return bail(fail(DSP_ERR_NOMEM, "scratch: %s", cudaGetErrorString(e)));
   int lo = 0, hi = 0;
@@ -353,11 +459,17 @@ extern "C" int dsp_rank_create(const dsp_rank_desc *d, dsp_rank **out) {
       cudaEventCreate(&r->ev_c1) != cudaSuccess ||
       cudaEventCreateWithFlags(&r->ev_zero, cudaEventDisableTiming) != cudaSuccess)
     return bail(fail(DSP_ERR_CUDA, "event create failed"));
+  const int n_seg = (int)r->segs.size();
   for (auto *v : {&r->ev_fetch, &r->ev_fetch_begin, &r->ev_seg_begin, &r->ev_seg_end}) {
-    v->assign((size_t)r->P, nullptr);
-    for (int k = 0; k < r->P; ++k)
+    const int n = (v == &r->ev_seg_begin || v == &r->ev_seg_end) ? std::max(r->P, n_seg) : r->P;
+    v->assign((size_t)n, nullptr);
+    for (int k = 0; k < n; ++k)
       if (cudaEventCreate(&(*v)[(size_t)k]) != cudaSuccess) return bail(fail(DSP_ERR_CUDA, "event create failed"));
   }
+  r->ev_group.assign(r->gfetch.size(), nullptr);
+  for (auto &ev : r->ev_group)
+    if (cudaEventCreateWithFlags(&ev, cudaEventDisableTiming) != cudaSuccess)
+      return bail(fail(DSP_ERR_CUDA, "event create failed"));
 
   // statistics
   auto &s = r->stats;
@@ -366,17 +478,19 @@ extern "C" int dsp_rank_create(const dsp_rank_desc *d, dsp_rank **out) {
   s.segments = 0;
   s.launches_per_step = 0;
   s.kernels_per_step = r->n_empty > 0;
-  for (int k = 0; k < r->P; ++k) {
+  for (int k = 0; k < n_seg; ++k) {
     const auto &op = r->segs[(size_t)k].op;
     if (op.units() > 0) {
       s.segments++;
       s.kernels_per_step += 1 + (op.n_split > 0);
     }
-    if (k > 0) {
-      s.kernels_per_step += r->fetch[(size_t)k].n_rows > 0;
-      s.launches_per_step += (int64_t)r->fetch[(size_t)k].bulk.size();
-    }
   }
+  for (int k = 1; k < r->P && k < (int)r->fetch.size(); ++k) {
+    s.kernels_per_step += r->fetch[(size_t)k].n_rows > 0;
+    s.launches_per_step += (int64_t)r->fetch[(size_t)k].bulk.size();
+  }
+  for (auto &F : r->gfetch) s.kernels_per_step += F.n_rows > 0;
+  s.timeline_len = std::max(r->P, n_seg);
   s.launches_per_step += s.kernels_per_step;
   for (int64_t t : r->owned) s.owned_rows += std::max<int64_t>(0, std::min<int64_t>(r->cpt, r->M - t * r->cpt));
   {
@@ -389,6 +503,7 @@ extern "C" int dsp_rank_create(const dsp_rank_desc *d, dsp_rank **out) {
                    (r->d_first_phase ? std::max<int64_t>(r->m_local, 1) : 0);
   for (auto &S : r->segs) s.device_bytes += S.op.device_bytes();
   for (auto &F : r->fetch) s.device_bytes += F.n_rows * 4;
+  for (auto &F : r->gfetch) s.device_bytes += F.n_rows * 4;
   *out = r;
   return DSP_OK;
 }
@@ -402,8 +517,11 @@ extern "C" void dsp_rank_destroy(dsp_rank *r) {
   for (int p = 0; p < r->P; ++p)
     if (r->peer_ipc[(size_t)p] && r->peer_B[(size_t)p]) cudaIpcCloseMemHandle((void *)r->peer_B[(size_t)p]);
   for (auto &S : r->segs) S.op.release();
-  for (auto &F : r->fetch)
-    if (F.d_rows) cudaFree(F.d_rows);
+  for (auto *v : {&r->fetch, &r->gfetch})
+    for (auto &F : *v)
+      if (F.d_rows) cudaFree(F.d_rows);
+  for (auto ev : r->ev_group)
+    if (ev) cudaEventDestroy(ev);
   if (r->B) cudaFree(r->B);
   if (r->C) cudaFree(r->C);
   if (r->scratch) cudaFree(r->scratch);
@@ -542,10 +660,91 @@ extern "C" int dsp_rank_download_c(dsp_rank *r, float *C_host, void *stream) {
   return DSP_OK;
 }
 
+namespace {
+
+// One step of the groups pipeline: bulk tiles, then the fetches of group 0 from every peer,
+// group 1, ... (group-major, so each fetch stream serves its peers' groups in order), while
+// the compute stream runs group g once the fetches of groups 0..g have landed.
+int step_groups(dsp_rank *r, cudaStream_t stream) {
+  const int P = r->P, G = r->n_groups;
+  for (int k = 1; k < P; ++k) {
+    bool any = !r->fetch[(size_t)k].bulk.empty();
+    for (int g = 0; g < G; ++g) any = any || r->gfetch[(size_t)g * P + k].n_rows > 0;
+    if (any && !r->peer_B[(size_t)((r->me + k) % P)])
+      return fail(DSP_ERR_STATE, "rank %d: B of peer %d not attached", r->me, (r->me + k) % P);
+  }
+  DSP_CUDA(cudaEventRecord(r->ev_start, stream));
+  DSP_CUDA(cudaStreamWaitEvent(r->compute, r->ev_start, 0));
+  for (auto s : r->fstreams) DSP_CUDA(cudaStreamWaitEvent(s, r->ev_start, 0));
+  std::vector<bool> has_fetch((size_t)P, false);
+  std::vector<std::vector<bool>> landed((size_t)G, std::vector<bool>((size_t)P, false));
+  for (int k = 1; k < P; ++k) {  // bulk tiles first, counted as group 0's
+    const auto &F = r->fetch[(size_t)k];
+    cudaStream_t fs = r->fstreams[(size_t)((k - 1) % r->n_streams)];
+    DSP_CUDA(cudaEventRecord(r->ev_fetch_begin[(size_t)k], fs));
+    if (F.bulk.empty()) continue;
+    const float *src = r->peer_B[(size_t)((r->me + k) % P)];
+    for (const auto &b : F.bulk) {
+      const size_t off = (size_t)b.first * r->dims;
+      DSP_CUDA(cudaMemcpyAsync(r->B + off, src + off, sizeof(float) * (size_t)b.second * r->dims, cudaMemcpyDefault,
+                               fs));
+    }
+    has_fetch[(size_t)k] = true;
+  }
+  for (int g = 0; g < G; ++g)
+    for (int k = 1; k < P; ++k) {
+      const auto &F = r->gfetch[(size_t)g * P + k];
+      cudaStream_t fs = r->fstreams[(size_t)((k - 1) % r->n_streams)];
+      if (F.n_rows) {
+        int rc = launch_gather_rows(r->B, r->peer_B[(size_t)((r->me + k) % P)], F.d_rows, F.n_rows, r->dims,
+                                    r->fetch_engine, r->d_err, fs);
+        if (rc) return rc;
+        has_fetch[(size_t)k] = true;
+      }
+      if (F.n_rows || (g == 0 && !r->fetch[(size_t)k].bulk.empty())) {
+        DSP_CUDA(cudaEventRecord(r->ev_group[(size_t)g * P + k], fs));
+        landed[(size_t)g][(size_t)k] = true;
+      }
+    }
+  for (int k = 1; k < P; ++k)
+    if (has_fetch[(size_t)k])
+      DSP_CUDA(cudaEventRecord(r->ev_fetch[(size_t)k], r->fstreams[(size_t)((k - 1) % r->n_streams)]));
+  DSP_CUDA(cudaEventRecord(r->ev_c0, r->compute));
+  int rc;
+  if (r->n_empty) {
+    DSP_CUDA(cudaStreamWaitEvent(r->side, r->ev_c0, 0));
+    if ((rc = launch_zero_rows(r->C, r->dims, r->d_empty, r->n_empty, r->dims, r->side))) return rc;
+    DSP_CUDA(cudaEventRecord(r->ev_zero, r->side));
+  }
+  r->seg_ran.assign(r->ev_seg_begin.size(), false);
+  for (int g = 0; g < G; ++g) {
+    for (int k = 1; k < P; ++k)
+      if (landed[(size_t)g][(size_t)k])
+        DSP_CUDA(cudaStreamWaitEvent(r->compute, r->ev_group[(size_t)g * P + k], 0));
+    const auto &op = r->segs[(size_t)g].op;
+    if (op.units() == 0) continue;
+    DSP_CUDA(cudaEventRecord(r->ev_seg_begin[(size_t)g], r->compute));
+    SpmmArgs sa = op.args(r->B, r->dims, r->C, r->dims, r->dims, r->scratch);
+    if ((rc = launch_spmm(sa, false, r->compute))) return rc;
+    DSP_CUDA(cudaEventRecord(r->ev_seg_end[(size_t)g], r->compute));
+    r->seg_ran[(size_t)g] = true;
+  }
+  r->fetch_ran = has_fetch;
+  if (r->n_empty) DSP_CUDA(cudaStreamWaitEvent(r->compute, r->ev_zero, 0));
+  DSP_CUDA(cudaEventRecord(r->ev_c1, r->compute));
+  for (int k = 1; k < P; ++k)
+    if (has_fetch[(size_t)k]) DSP_CUDA(cudaStreamWaitEvent(stream, r->ev_fetch[(size_t)k], 0));
+  DSP_CUDA(cudaStreamWaitEvent(stream, r->ev_c1, 0));
+  return DSP_OK;
+}
+
+}  // namespace
+
 extern "C" int dsp_rank_step(dsp_rank *r, void *stream_v) {
   DSP_TRY_ARG(r, "dsp_rank_step: null rank");
   DeviceGuard g(r->device);
   cudaStream_t stream = (cudaStream_t)stream_v;
+  if (r->n_groups > 0) return step_groups(r, stream);
   for (int k = 1; k < r->P; ++k) {
     const auto &F = r->fetch[(size_t)k];
     if ((F.n_rows || !F.bulk.empty()) && !r->peer_B[(size_t)r->segs[(size_t)k].owner])
@@ -625,9 +824,10 @@ extern "C" int dsp_rank_last_compute_ms(dsp_rank *r, float *ms) {
 }
 
 extern "C" int dsp_rank_last_timeline(dsp_rank *r, float *ms, int cap) {
-  DSP_TRY_ARG(r && ms && cap >= 4 * r->P, "dsp_rank_last_timeline: need %d floats", r ? 4 * r->P : 0);
+  const int n = r ? (int)r->stats.timeline_len : 0;
+  DSP_TRY_ARG(r && ms && cap >= 4 * n, "dsp_rank_last_timeline: need %d floats", 4 * n);
   DeviceGuard g(r->device);
-  for (int k = 0; k < r->P; ++k) {
+  for (int k = 0; k < n; ++k) {
     float *o = ms + 4 * k;
     o[0] = o[1] = o[2] = o[3] = -1.f;
     if (k < (int)r->fetch_ran.size() && r->fetch_ran[(size_t)k]) {

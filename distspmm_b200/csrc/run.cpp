@@ -70,6 +70,7 @@ extern "C" int dsp_run(const dsp_args *A, dsp_report *rep) {
   const int pipeline = !pipe_env                        ? DSP_PIPELINE_AUTO
                        : strcmp(pipe_env, "rows") == 0  ? DSP_PIPELINE_ROWS
                        : strcmp(pipe_env, "split") == 0 ? DSP_PIPELINE_SPLIT
+                       : strcmp(pipe_env, "groups") == 0 ? DSP_PIPELINE_GROUPS
                                                         : DSP_PIPELINE_AUTO;
 
   // 2. 1-D row partition (src/dist_spmm_node.cu:82-99)

@@ -61,6 +61,7 @@ extern "C" int dsp_run_rank(const dsp_args *A, int me, int P, int device, dsp_st
   const int pipeline = !pipe_env                        ? DSP_PIPELINE_AUTO
                        : strcmp(pipe_env, "rows") == 0  ? DSP_PIPELINE_ROWS
                        : strcmp(pipe_env, "split") == 0 ? DSP_PIPELINE_SPLIT
+                       : strcmp(pipe_env, "groups") == 0 ? DSP_PIPELINE_GROUPS
                                                         : DSP_PIPELINE_AUTO;
   int rc;
   double t0;

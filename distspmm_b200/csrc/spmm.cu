@@ -723,12 +723,13 @@ WarpShape warp_shape(int N, const float *B, int64_t ldb, const float *C, int64_t
   WarpShape w;
   if (!env_on || N <= 0 || N % 128 != 0 || ldb % 4 != 0 || ldc % 4 != 0 || !aligned(B, 16) || !aligned(C, 16))
     return w;
-  // One float4 per lane (128 columns per launch row of blocks, blockIdx.y covering wider B)
-  // and 4 nonzeros per step, with the registers held to 48 so that 5 blocks (40 warps) fit
-  // an SM: measured best on R-MAT (scale 20: 1.32 ms against 1.46 uncapped and 1.92 with 8
-  // nonzeros per step; scale 24: 26.9 against 29.4 ms).
+  // 4 nonzeros per step. N = 128: one float4 per lane, registers held to 48 so that 5 blocks
+  // (40 warps) fit an SM (R-MAT scale 20: 1.32 ms against 1.46 uncapped and 1.92 with 8
+  // nonzeros per step; scale 24: 26.9 against 29.4 ms). Wider B: 2 or 4 float4 per lane
+  // (one pass over A for 256 / 512 columns; scale 20: N = 256 2.38 ms against 2.66 with one
+  // float4 and two column blocks, N = 512 4.97 against 5.90), blockIdx.y covering the rest.
   const int n128 = N / 128;
-  const int vpl = env_vpl > 0 && n128 % env_vpl == 0 ? env_vpl : 1;
+  const int vpl = env_vpl > 0 && n128 % env_vpl == 0 ? env_vpl : n128 % 4 == 0 ? 4 : n128 % 2 == 0 ? 2 : 1;
   const int u = env_u > 0 ? env_u : 4;
   const int dflt_mb = vpl == 1 && u == 4 ? 5 : vpl == 2 && u == 4 ? 3 : 1;
   const int mb = env_mb > 0 && warp_kernel_for(vpl, u, false, env_mb) ? env_mb : dflt_mb;

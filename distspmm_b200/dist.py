@@ -52,7 +52,7 @@ def global_plan(tilings: list, task_dist: int, n_rolls: int) -> GlobalPlan:
 # ---------------------------------------------------------------------------- rank
 
 FETCH_ENGINES = {"lsu": 0, "tma": 1}  # DSP_FETCH_LSU / DSP_FETCH_TMA
-PIPELINES = {"auto": 0, "rows": 1, "split": 2}  # DSP_PIPELINE_*
+PIPELINES = {"auto": 0, "rows": 1, "split": 2, "groups": 3}  # DSP_PIPELINE_*
 
 
 class Rank:
@@ -60,7 +60,7 @@ class Rank:
 
     def __init__(self, local: Csr, rank: int, world: int, device: int, dims: int, M: int, m_lb: int,
                  plan: GlobalPlan, n_slice: np.ndarray, sparse: np.ndarray, n_streams: int = 4,
-                 fetch_engine: str = "lsu", pipeline: str = "auto"):
+                 fetch_engine: str = "lsu", pipeline: str = "auto", groups: int = 0):
         self.rank, self.world, self.device, self.dims, self.M = rank, world, device, dims, M
         self.m_local = local.num_rows
         self.m_lb = m_lb
@@ -81,6 +81,7 @@ class Rank:
         d.n_slice = self._keep[2].ctypes.data_as(P(c_i32))
         d.fetch_engine = FETCH_ENGINES[fetch_engine]
         d.pipeline = PIPELINES[pipeline]
+        d.groups = groups
         h = c_vp()
         call("dsp_rank_create", ctypes.byref(d), ctypes.byref(h))
         self._h = h
@@ -158,12 +159,13 @@ class Rank:
         return float(ms.value)
 
     def timeline(self) -> list:
-        """Last step: per ring position k, (fetch_begin, fetch_end, seg_begin, seg_end) in ms
-        from the step start (None where nothing ran)."""
-        buf = (c_f32 * (4 * self.world))()
-        call("dsp_rank_last_timeline", self._h, buf, 4 * self.world)
+        """Last step: per entry k, (fetch_begin, fetch_end of ring position k, seg_begin,
+        seg_end of phase or row group k) in ms from the step start (None where nothing ran)."""
+        n = self.stats()["timeline_len"]
+        buf = (c_f32 * (4 * n))()
+        call("dsp_rank_last_timeline", self._h, buf, 4 * n)
         out = []
-        for k in range(self.world):
+        for k in range(n):
             out.append(tuple(None if buf[4 * k + i] < 0 else round(float(buf[4 * k + i]), 4) for i in range(4)))
         return out
 
@@ -203,12 +205,13 @@ def fetch_view(plan: GlobalPlan, tiling, scope: str = "node") -> GlobalPlan:
 
 def make_rank(local: Csr, rank: int, world: int, device: int, dims: int, M: int, m_lb: int, tiling,
               plan: GlobalPlan, comm_type: int, platform: str = "h100", n_streams: int = 4,
-              fetch_engine: str = "lsu", fetch_scope: str = "node", pipeline: str = "auto") -> Rank:
+              fetch_engine: str = "lsu", fetch_scope: str = "node", pipeline: str = "auto",
+              groups: int = 0) -> Rank:
     """Selector (CommMan_hp ctor, src/comm_man.h:341-410) + rank construction."""
     view = fetch_view(plan, tiling, fetch_scope)
     sparse = planner.comm_select(comm_type, dims, view.n_col, tiling.n_slice, platform)
     r = Rank(local, rank, world, device, dims, M, m_lb, view, tiling.n_slice, sparse, n_streams, fetch_engine,
-             pipeline)
+             pipeline, groups)
     r.sparse = sparse
     r.n_slice = tiling.n_slice
     r.n_col = view.n_col
@@ -241,7 +244,7 @@ class LocalGroup:
 def build_local_group(g: Csr, world: int, devices, dims: int, n_rolls: int = 4, task_dist: int = 2,
                       comm_type: int = 2, platform: str = "h100", n_streams: int = 4,
                       fetch_engine: str = "lsu", partition: str = "rows",
-                      fetch_scope: str = "node", pipeline: str = "auto") -> LocalGroup:
+                      fetch_scope: str = "node", pipeline: str = "auto", groups: int = 0) -> LocalGroup:
     """All `world` ranks of the pipeline in this process; devices[p] is rank p's GPU
     (ranks may share one). Peers read each other's B directly (same device, or peer
     access between devices)."""
@@ -252,7 +255,7 @@ def build_local_group(g: Csr, world: int, devices, dims: int, n_rolls: int = 4, 
     tilings = [planner.tile(loc, T) for loc in locals_]
     plan = global_plan(tilings, task_dist, n_rolls)
     ranks = [make_rank(locals_[p], p, world, devices[p], dims, M, bounds[p][0], tilings[p], plan, comm_type,
-                       platform, n_streams, fetch_engine, fetch_scope, pipeline) for p in range(world)]
+                       platform, n_streams, fetch_engine, fetch_scope, pipeline, groups) for p in range(world)]
     for p in range(world):
         for q in range(world):
             if p != q:

@@ -315,6 +315,7 @@ typedef struct dsp_rank_desc {
   const int32_t *n_slice;        /* [T] n_slice_list of this rank               */
   int fetch_engine;              /* DSP_FETCH_LSU (default) or DSP_FETCH_TMA     */
   int pipeline;                  /* DSP_PIPELINE_* (0 = pick from the matrix)    */
+  int groups;                    /* DSP_PIPELINE_GROUPS: row groups (0 = 8)      */
 } dsp_rank_desc;
 
 /* How a rank's nonzeros are cut into phases, phase k running once the fetches of ring
@@ -326,10 +327,20 @@ typedef struct dsp_rank_desc {
  *          loop (src/dist_spmm_node.cu:329-394): a row is written in its first phase and
  *          accumulated in later ones, so compute overlaps every fetch; best when nearly all
  *          rows need remote tiles (power-law graphs).
- *   AUTO   SPLIT when less than half the nonzeros fall in ROWS's phase 0. */
+ *   GROUPS (no counterpart in the reference) the local rows in `groups` contiguous groups
+ *          of equal work; every remote row is fetched with the first group that needs it,
+ *          from every peer at once, and group g runs once the fetches of groups 0..g have
+ *          landed, so later groups' fetches hide behind earlier groups' SpMM. Each rank
+ *          fetches only the rows its own nonzeros need (the node-merged lists are not
+ *          used). Best on power-law graphs, whose rows need every peer: at P = 8 the first
+ *          of 8 groups needs ~40 % of a rank's remote rows and each later group 5-16 %.
+ *   AUTO   ROWS when at least half the nonzeros fall in its phase 0; otherwise SPLIT when
+ *          the owned tiles hold enough work and the accumulated pieces are long, else
+ *          GROUPS. */
 #define DSP_PIPELINE_AUTO 0
 #define DSP_PIPELINE_ROWS 1
 #define DSP_PIPELINE_SPLIT 2
+#define DSP_PIPELINE_GROUPS 3
 
 /* Sparse-fetch engines: LSU = warps with 128-bit peer loads, one block per SM next to the
  * SpMM; TMA = per-row cp.async.bulk copies through a shared-memory ring (no multicast). */
@@ -348,8 +359,9 @@ typedef struct dsp_rank_stats {
   int64_t launches_per_step; /* kernels + copies enqueued per step               */
   int64_t kernels_per_step;  /* of which kernels of this library                  */
   int64_t device_bytes;      /* device memory held by the rank                   */
-  int64_t pipeline;          /* DSP_PIPELINE_ROWS or DSP_PIPELINE_SPLIT in use   */
+  int64_t pipeline;          /* DSP_PIPELINE_ROWS, _SPLIT or _GROUPS in use      */
   int64_t phase0_nnz;        /* nonzeros computed before any fetch lands         */
+  int64_t timeline_len;      /* entries of dsp_rank_last_timeline (max(P, groups)) */
 } dsp_rank_stats;
 
 int dsp_rank_create(const dsp_rank_desc *d, dsp_rank **out);
@@ -404,9 +416,10 @@ int dsp_rank_download_c(dsp_rank *r, float *C_host, void *stream);
  * stream (valid after the step completed). */
 int dsp_rank_last_compute_ms(dsp_rank *r, float *ms);
 /* Timeline of the last step (valid after it completed), ms from the step's start, 4 floats
- * per ring position k = 0..P-1: fetch begin, fetch end (peer (me+k)%P), segment begin,
- * segment end; -1 where nothing ran. cap >= 4*P. Shows how much of the fetch the SpMM
- * segments hid (the reference measures only whole reps, src/dist_spmm_node.cu:329-394). */
+ * per entry k < dsp_rank_stats.timeline_len: fetch begin, fetch end of ring position k (peer
+ * (me+k)%P, k < P), segment begin, segment end of phase (or row group) k; -1 where nothing
+ * ran. cap >= 4 * timeline_len. Shows how much of the fetch the SpMM segments hid (the
+ * reference measures only whole reps, src/dist_spmm_node.cu:329-394). */
 int dsp_rank_last_timeline(dsp_rank *r, float *ms, int cap);
 
 /* ---------------------------------------------------------------- whole pipeline */

@@ -25,11 +25,11 @@ def _devices(world):
 
 
 def _run_group(A, world, dims, rolls, task_dist, comm_type, seed=21, poison=True, fetch_engine="lsu",
-               partition="rows", fetch_scope="node", pipeline="auto"):
+               partition="rows", fetch_scope="node", pipeline="auto", groups=0):
     import torch
     from distspmm_b200.dist import build_local_group
     g = build_local_group(A, world, _devices(world), dims, rolls, task_dist, comm_type, fetch_engine=fetch_engine,
-                          partition=partition, fetch_scope=fetch_scope, pipeline=pipeline)
+                          partition=partition, fetch_scope=fetch_scope, pipeline=pipeline, groups=groups)
     for r in g.ranks:
         if poison:
             r.poison_remote()
@@ -165,6 +165,37 @@ def test_group_parity_pipelines(gpu, rmat12, pipeline, world, comm_type, partiti
     _check(rmat12, C, 128)
     assert all(r.stats()["pipeline"] == (1 if pipeline == "rows" else 2) for r in g.ranks)
     g.close()
+
+
+@pytest.mark.parametrize("world,comm_type,partition,groups", [
+    (2, 2, "rows", 0), (3, 1, "balanced", 3), (4, 0, "balanced", 8), (8, 2, "balanced", 8), (8, 1, "rows", 1),
+    (2, 1, "balanced", 5000)])
+def test_group_parity_row_groups(gpu, rmat12, world, comm_type, partition, groups):
+    """Row groups: every remote row arrives with the first group that needs it and each group
+    waits only for its own and earlier groups' fetches (remote rows NaN-poisoned before the
+    step, so a row used before it landed shows up). Includes one group, more groups than
+    rows, and bulk-only fetches."""
+    g, C = _run_group(rmat12, world, 128, 4, 2, comm_type, partition=partition, fetch_scope="rank",
+                      pipeline="groups", groups=groups)
+    _check(rmat12, C, 128)
+    for r in g.ranks:
+        st = r.stats()
+        assert st["pipeline"] == 3
+        assert st["timeline_len"] == max(world, min(groups or 8, st["m_local"]) if st["m_local"] else world)
+        tl = r.timeline()
+        # a group's SpMM starts after the fetch kernels it depends on were issued: groups
+        # run in order on the compute stream
+        segs = [t for t in tl if t[2] is not None]
+        assert all(a[3] <= b[2] + 1e-3 for a, b in zip(segs, segs[1:]))
+    g.close()
+
+
+def test_group_row_groups_stencil_and_widths(gpu):
+    A = d.gen_stencil27(16, seed=9)
+    for dims in (64, 128, 256):
+        g, C = _run_group(A, 4, dims, 2, 2, 2, partition="balanced", fetch_scope="rank", pipeline="groups")
+        _check(A, C, dims)
+        g.close()
 
 
 @pytest.mark.parametrize("dims", [4, 100, 256])
