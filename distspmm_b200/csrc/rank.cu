@@ -218,10 +218,7 @@ int build_phases(dsp_rank *r, const dsp_csr *a, int pipeline, int groups) {
                    : DSP_PIPELINE_GROUPS;
   if (P == 1 || P > 64) pipeline = DSP_PIPELINE_ROWS;
   r->pipeline = pipeline;
-  if (pipeline == DSP_PIPELINE_GROUPS) {
-    r->stats.phase0_nnz = 0;
-    return build_groups(r, a, groups);
-  }
+  if (pipeline == DSP_PIPELINE_GROUPS) return build_groups(r, a, groups);
   if (pipeline == DSP_PIPELINE_SPLIT) {
     r->stats.phase0_nnz = local_nnz;
     return build_split_phases(r, a, first);
@@ -292,20 +289,23 @@ int build_fetch(dsp_rank *r, const dsp_rank_desc *d) {
   return DSP_OK;
 }
 
-// Groups pipeline: the local rows in G contiguous groups of equal cost (nonzeros + rows),
-// one operand each (its rows listed with their own ids, so banded groups keep the diagonal
-// form); rows without nonzeros are zero-filled apart, as in the other pipelines.
+// Groups pipeline. Segment 0 holds the nonzeros of every row whose column tiles this rank
+// owns (no fetch needed: it runs while group 0's rows arrive) and writes those rows; the
+// local rows are cut into G contiguous groups of equal cost (nonzeros + rows), and segment
+// g + 1 holds group g's remote nonzeros, adding to rows segment 0 wrote (first_phase) and
+// writing the others. Every row is thus written once and read back at most once.
 int build_groups(dsp_rank *r, const dsp_csr *a, int groups) {
   const int64_t m = a->num_rows;
-  const int G = (int)std::max<int64_t>(1, std::min<int64_t>(groups > 0 ? groups : 8, std::max<int64_t>(m, 1)));
+  // at most 253 groups: segment numbers (first_phase) are bytes, 255 meaning "no nonzeros"
+  const int G = (int)std::max<int64_t>(1, std::min<int64_t>({groups > 0 ? groups : 8, std::max<int64_t>(m, 1), 253}));
+  const int me = r->me;
   r->n_groups = G;
-  r->segs.assign((size_t)G, dsp_rank::Segment());
+  r->segs.assign((size_t)G + 1, dsp_rank::Segment());
   r->group_end.assign((size_t)G, m);
   const int64_t total = a->nnz + m;
   int64_t rb = 0;
-  std::vector<int32_t> ids;
   for (int g = 0; g < G; ++g) {
-    // first row of group g + 1: cost(indptr[i] + i) reaches (g + 1) / G of the total
+    // first row of group g + 1: cost (indptr[i] + i) reaches (g + 1) / G of the total
     const int64_t target = (total * (g + 1) + G - 1) / G;
     int64_t lo = rb, hi = m;
     while (lo < hi) {
@@ -313,21 +313,61 @@ int build_groups(dsp_rank *r, const dsp_csr *a, int groups) {
       if (a->indptr[mid] + mid >= target) hi = mid;
       else lo = mid + 1;
     }
-    const int64_t re = g == G - 1 ? m : lo;
-    auto &S = r->segs[(size_t)g];
-    S.owner = -1;
-    const int64_t nz = a->indptr[re] - a->indptr[rb];
-    if (re > rb && nz > 0) {
-      ids.resize((size_t)(re - rb));
-      for (int64_t i = rb; i < re; ++i) ids[(size_t)(i - rb)] = (int32_t)i;
-      int rc = S.op.upload(r->device, m, r->M, a->indptr + rb, ids.data(), re - rb, a->indices, a->values,
-                           a->indptr[rb], nz, r->dims, false);
-      if (rc) return rc;
-      r->scratch_floats = std::max(r->scratch_floats, S.op.pieces * (int64_t)r->dims);
-    }
-    r->group_end[(size_t)g] = re;
-    rb = re;
+    r->group_end[(size_t)g] = g == G - 1 ? m : lo;
+    rb = r->group_end[(size_t)g];
   }
+  // per row: owned / remote nonzeros; first_phase = 0 when segment 0 writes the row
+  auto owned = [&](int64_t c) { return r->remap[(size_t)(c / r->cpt)] == me; };
+  std::vector<uint8_t> fp((size_t)std::max<int64_t>(m, 1), 0xff);
+  std::vector<int32_t> grp((size_t)std::max<int64_t>(m, 1), 0);
+  {
+    int g = 0;
+    for (int64_t i = 0; i < m; ++i) {
+      while (g + 1 < G && i >= r->group_end[(size_t)g]) ++g;
+      grp[(size_t)i] = g;
+    }
+  }
+  std::vector<uint8_t> has_own((size_t)std::max<int64_t>(m, 1), 0), has_rem((size_t)std::max<int64_t>(m, 1), 0);
+  parallel_for(m, [&](int64_t b, int64_t e) {
+    for (int64_t i = b; i < e; ++i)
+      for (int64_t j = a->indptr[i]; j < a->indptr[i + 1]; ++j) (owned(a->indices[j]) ? has_own : has_rem)[(size_t)i] = 1;
+  }, 1024);
+  int64_t own_nnz = 0;
+  for (int64_t i = 0; i < m; ++i) {
+    if (has_own[(size_t)i]) fp[(size_t)i] = 0;
+    else if (has_rem[(size_t)i]) fp[(size_t)i] = (uint8_t)(grp[(size_t)i] + 1);
+  }
+  int rc = dev_upload(&r->d_first_phase, fp.data(), fp.size());
+  if (rc) return rc;
+  // segment k: listed rows and their nonzeros (owned ones for k = 0, group k - 1's remote ones)
+  for (int k = 0; k <= G; ++k) {
+    const int64_t r0 = k == 0 ? 0 : (k == 1 ? 0 : r->group_end[(size_t)k - 2]);
+    const int64_t r1 = k == 0 ? m : r->group_end[(size_t)k - 1];
+    std::vector<int32_t> rows;
+    std::vector<int64_t> ptr(1, 0), idx;
+    std::vector<float> val;
+    for (int64_t i = r0; i < r1; ++i) {
+      const int64_t before = (int64_t)idx.size();
+      for (int64_t j = a->indptr[i]; j < a->indptr[i + 1]; ++j)
+        if (owned(a->indices[j]) == (k == 0)) {
+          idx.push_back(a->indices[j]);
+          val.push_back(a->values[j]);
+        }
+      if ((int64_t)idx.size() > before) {
+        rows.push_back((int32_t)i);
+        ptr.push_back((int64_t)idx.size());
+      }
+    }
+    if (k == 0) own_nnz = (int64_t)idx.size();
+    auto &S = r->segs[(size_t)k];
+    S.owner = k == 0 ? me : -1;
+    if (idx.empty()) continue;
+    rc = S.op.upload(r->device, m, r->M, ptr.data(), rows.data(), (int64_t)rows.size(), idx.data(), val.data(), 0,
+                     ptr.back(), r->dims, false);
+    if (rc) return rc;
+    r->scratch_floats = std::max(r->scratch_floats, S.op.pieces * (int64_t)r->dims);
+  }
+  r->stats.phase0_nnz = own_nnz;
   return DSP_OK;
 }
 
@@ -664,7 +704,8 @@ namespace {
 
 // One step of the groups pipeline: bulk tiles, then the fetches of group 0 from every peer,
 // group 1, ... (group-major, so each fetch stream serves its peers' groups in order), while
-// the compute stream runs group g once the fetches of groups 0..g have landed.
+// the compute stream runs segment 0 (owned columns) at once and group g's remote nonzeros
+// once the fetches of groups 0..g have landed.
 int step_groups(dsp_rank *r, cudaStream_t stream) {
   const int P = r->P, G = r->n_groups;
   for (int k = 1; k < P; ++k) {
@@ -717,17 +758,20 @@ int step_groups(dsp_rank *r, cudaStream_t stream) {
     DSP_CUDA(cudaEventRecord(r->ev_zero, r->side));
   }
   r->seg_ran.assign(r->ev_seg_begin.size(), false);
-  for (int g = 0; g < G; ++g) {
-    for (int k = 1; k < P; ++k)
-      if (landed[(size_t)g][(size_t)k])
-        DSP_CUDA(cudaStreamWaitEvent(r->compute, r->ev_group[(size_t)g * P + k], 0));
-    const auto &op = r->segs[(size_t)g].op;
+  for (int k = 0; k <= G; ++k) {  // segment 0: owned columns; segment g + 1: group g's remote ones
+    if (k > 0)
+      for (int q = 1; q < P; ++q)
+        if (landed[(size_t)k - 1][(size_t)q])
+          DSP_CUDA(cudaStreamWaitEvent(r->compute, r->ev_group[(size_t)(k - 1) * P + q], 0));
+    const auto &op = r->segs[(size_t)k].op;
     if (op.units() == 0) continue;
-    DSP_CUDA(cudaEventRecord(r->ev_seg_begin[(size_t)g], r->compute));
+    DSP_CUDA(cudaEventRecord(r->ev_seg_begin[(size_t)k], r->compute));
     SpmmArgs sa = op.args(r->B, r->dims, r->C, r->dims, r->dims, r->scratch);
+    sa.first_phase = r->d_first_phase;  // rows written by segment 0 are accumulated
+    sa.phase = k;
     if ((rc = launch_spmm(sa, false, r->compute))) return rc;
-    DSP_CUDA(cudaEventRecord(r->ev_seg_end[(size_t)g], r->compute));
-    r->seg_ran[(size_t)g] = true;
+    DSP_CUDA(cudaEventRecord(r->ev_seg_end[(size_t)k], r->compute));
+    r->seg_ran[(size_t)k] = true;
   }
   r->fetch_ran = has_fetch;
   if (r->n_empty) DSP_CUDA(cudaStreamWaitEvent(r->compute, r->ev_zero, 0));

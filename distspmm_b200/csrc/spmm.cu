@@ -503,27 +503,29 @@ __device__ __forceinline__ void dia_run(const SpmmArgs &a, const float *sv, int 
 #pragma unroll
   for (int l = 0; l < L; ++l) all = all && pb[l] == 0xffu;
   float4 b[R + L - 1];
-#pragma unroll
-  for (int k = 0; k < R + L - 1; ++k) {
-    uint32_t need = all ? 1u : 0u;  // some present entry of the block uses B row jb + k
-#pragma unroll
-    for (int l = 0; l < L; ++l)
-      if (k - l >= 0 && k - l < R) need |= (pb[l] >> (k - l)) & 1u;
-    b[k] = need ? V::ldg(a.B + (jb + k) * a.ldb + col0, pol) : V::zero();
-  }
   if (all) {
+#pragma unroll
+    for (int k = 0; k < R + L - 1; ++k) b[k] = V::ldg(a.B + (jb + k) * a.ldb + col0, pol);
 #pragma unroll
     for (int k = 0; k < R + L - 1; ++k)
 #pragma unroll
       for (int l = 0; l < L; ++l)
         if (k - l >= 0 && k - l < R) V::fma(acc[k - l], sv[(d0 + l) * R + k - l], b[k]);
-  } else {
-#pragma unroll
-    for (int k = 0; k < R + L - 1; ++k)
-#pragma unroll
-      for (int l = 0; l < L; ++l)
-        if (k - l >= 0 && k - l < R && ((pb[l] >> (k - l)) & 1u)) V::fma(acc[k - l], sv[(d0 + l) * R + k - l], b[k]);
+    return;
   }
+#pragma unroll
+  for (int k = 0; k < R + L - 1; ++k) {
+    uint32_t need = 0;  // some present entry of the block uses B row jb + k
+#pragma unroll
+    for (int l = 0; l < L; ++l)
+      if (k - l >= 0 && k - l < R) need |= (pb[l] >> (k - l)) & 1u;
+    b[k] = need ? V::ldg(a.B + (jb + k) * a.ldb + col0, pol) : V::zero();
+  }
+#pragma unroll
+  for (int k = 0; k < R + L - 1; ++k)
+#pragma unroll
+    for (int l = 0; l < L; ++l)
+      if (k - l >= 0 && k - l < R && ((pb[l] >> (k - l)) & 1u)) V::fma(acc[k - l], sv[(d0 + l) * R + k - l], b[k]);
 }
 
 template <bool kAccum>

@@ -327,13 +327,16 @@ typedef struct dsp_rank_desc {
  *          loop (src/dist_spmm_node.cu:329-394): a row is written in its first phase and
  *          accumulated in later ones, so compute overlaps every fetch; best when nearly all
  *          rows need remote tiles (power-law graphs).
- *   GROUPS (no counterpart in the reference) the local rows in `groups` contiguous groups
- *          of equal work; every remote row is fetched with the first group that needs it,
- *          from every peer at once, and group g runs once the fetches of groups 0..g have
- *          landed, so later groups' fetches hide behind earlier groups' SpMM. Each rank
- *          fetches only the rows its own nonzeros need (the node-merged lists are not
- *          used). Best on power-law graphs, whose rows need every peer: at P = 8 the first
- *          of 8 groups needs ~40 % of a rank's remote rows and each later group 5-16 %.
+ *   GROUPS (no counterpart in the reference) first the nonzeros of every row whose tiles
+ *          this rank owns (no fetch needed), then the local rows in `groups` contiguous
+ *          groups of equal work, each group's remote nonzeros added to those rows: every
+ *          remote row is fetched with the first group that needs it, from every peer at
+ *          once, and group g runs once the fetches of groups 0..g have landed, so the
+ *          fetches hide behind the owned-column pass and earlier groups' SpMM; a row is
+ *          written once and read back at most once. Each rank fetches only the rows its own
+ *          nonzeros need (the node-merged lists are not used). For power-law graphs, whose
+ *          rows need every peer: at P = 8 the first of 8 groups needs ~40 % of a rank's
+ *          remote rows and each later group 5-16 %.
  *   AUTO   ROWS when at least half the nonzeros fall in its phase 0; otherwise SPLIT when
  *          the owned tiles hold enough work and the accumulated pieces are long, else
  *          GROUPS. */

@@ -171,17 +171,20 @@ def test_group_parity_pipelines(gpu, rmat12, pipeline, world, comm_type, partiti
     (2, 2, "rows", 0), (3, 1, "balanced", 3), (4, 0, "balanced", 8), (8, 2, "balanced", 8), (8, 1, "rows", 1),
     (2, 1, "balanced", 5000)])
 def test_group_parity_row_groups(gpu, rmat12, world, comm_type, partition, groups):
-    """Row groups: every remote row arrives with the first group that needs it and each group
-    waits only for its own and earlier groups' fetches (remote rows NaN-poisoned before the
-    step, so a row used before it landed shows up). Includes one group, more groups than
-    rows, and bulk-only fetches."""
+    """Row groups: the owned-column nonzeros of every row run first, then each group's remote
+    nonzeros (added to the rows the first segment wrote); every remote row arrives with the
+    first group that needs it and each group waits only for its own and earlier groups'
+    fetches (remote rows NaN-poisoned before the step, so a row used before it landed shows
+    up). Includes one group, more groups than the byte-sized segment ids allow, and
+    bulk-only fetches."""
     g, C = _run_group(rmat12, world, 128, 4, 2, comm_type, partition=partition, fetch_scope="rank",
                       pipeline="groups", groups=groups)
     _check(rmat12, C, 128)
     for r in g.ranks:
         st = r.stats()
         assert st["pipeline"] == 3
-        assert st["timeline_len"] == max(world, min(groups or 8, st["m_local"]) if st["m_local"] else world)
+        G = min(groups or 8, max(st["m_local"], 1), 253)
+        assert st["timeline_len"] == max(world, G + 1)  # segment 0 (owned columns) + one per group
         tl = r.timeline()
         # a group's SpMM starts after the fetch kernels it depends on were issued: groups
         # run in order on the compute stream
