@@ -86,6 +86,8 @@ def parse_args(argv=None):
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-flush", action="store_true")
     ap.add_argument("--no-cusparse", action="store_true", help="skip the cuSPARSE comparison arm (N = 1)")
+    ap.add_argument("--no-ref-semantics", action="store_true",
+                    help="skip the N > 1 measurement under the reference's partition and merged fetch lists")
     ap.add_argument("--check-frac", type=float, default=0.01, help="fraction of each rank's rows checked")
     ap.add_argument("--profile", action="store_true",
                     help="short run for a profiler: warmup + steps only, no e2e / CPU baseline / clocks")
@@ -326,14 +328,15 @@ def load_local(a, rank, world, comm):
     """This rank's rows. N = 1: the generated matrix itself. N > 1: rank 0 generates the
     matrix once and writes the reference's binary CSR files to tmpfs; every rank reads the
     row pointer, finds its rows (planner.bounds) and reads only those (load_rows).
-    Returns (local, M, nnz, lb, ub, cleanup)."""
+    Returns (local, M, nnz, lb, ub, cleanup, rows_for): rows_for(partition) reads this
+    rank's rows under another partition (N > 1; None at N = 1)."""
     import numpy as np
 
     import distspmm_b200 as d
     from distspmm_b200 import planner
     if world == 1:
         A = make_workload(a)
-        return A, A.num_rows, A.nnz, 0, A.num_rows, None
+        return A, A.num_rows, A.nnz, 0, A.num_rows, None, None
     import torch.distributed as dist
     box = [None]
     if rank == 0:
@@ -359,7 +362,11 @@ def load_local(a, rank, world, comm):
             for f in os.listdir(tmp):
                 os.unlink(os.path.join(tmp, f))
             os.rmdir(tmp)
-    return local, M, nnz, lb, ub, cleanup
+
+    def rows_for(partition):
+        lb2, ub2 = planner.bounds(g, world, rank, partition)
+        return d.load_rows(prefix, lb2, ub2), lb2, ub2
+    return local, M, nnz, lb, ub, cleanup, rows_for
 
 
 def check_c(a, local, C_rows_of, rank):
@@ -452,7 +459,7 @@ def main(argv=None):
             comm.barrier()
 
     t_setup = time.perf_counter()
-    local, M, nnz, lb, ub, cleanup = load_local(a, rank, world, comm)
+    local, M, nnz, lb, ub, cleanup, rows_for = load_local(a, rank, world, comm)
     if comm is None:
         tiling = planner.tile(local, a.n_rolls)
         plan = global_plan([tiling], a.task_dist, a.n_rolls)
@@ -692,9 +699,49 @@ def main(argv=None):
         "wall_s_timed_region": round(wall, 3), "setup_s": round(setup_s, 1),
         "gather": gather,
     }
+    R.close()
+    # N > 1: the reference's own data movement on the same matrix — equal-row partition
+    # (src/dist_spmm_node.cu:85-93), node-merged fetch lists (src/utils.h:439-547) and its
+    # per-tile accumulation in ring order (the split pipeline, :329-394) — timed the same
+    # way, labelled beside the line's own (work-balanced rows, per-rank lists, AUTO pipeline)
+    if comm is not None and not a.profile and not a.no_ref_semantics:
+        local2, lb2, ub2 = rows_for("rows")
+        tiling2, plan2 = distributed_plan(comm, local2, a.n_rolls, a.task_dist)
+        R2 = make_rank(local2, rank, world, local_rank, a.dims, M, lb2, tiling2, plan2, a.comm_type, a.platform,
+                       a.fetch_streams, fetch_scope="node", pipeline="split")
+        connect_peers(comm, R2)
+        R2.fill_b(a.seed + 1, s.cuda_stream)
+        torch.cuda.synchronize(dev)
+        comm.barrier()
+        for _ in range(a.warmup):
+            R2.step(s.cuda_stream)
+        torch.cuda.synchronize(dev)
+        comm.barrier()
+        ms2 = []
+        for _ in range(a.steps):
+            flush_l2()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(s)
+            R2.step(s.cuda_stream)
+            e1.record(s)
+            e1.synchronize()
+            ms2.append(e0.elapsed_time(e1))
+        torch.cuda.synchronize(dev)
+        comm.barrier()
+        R2.check_error()
+        st2 = R2.stats()
+        t2 = comm.allreduce_max(statistics.mean(ms2))
+        f2 = comm.allreduce_sum_i64(st2["fetch_bytes"])
+        nnz_max = comm.allreduce_max(float(st2["nnz_local"]))
+        R2.close()
+        line["reference_semantics"] = {
+            "partition": "rows (ceil(M/P) rows per rank)", "fetch_scope": "node (merged lists)",
+            "pipeline": "split (per ring position, rows accumulated)",
+            "value": round(2.0 * nnz * a.dims / (t2 * 1e-3) / 1e9, 3), "unit": UNIT, "ms_per_step": round(t2, 4),
+            "fetched_bytes_per_step": f2, "max_rank_nnz": int(nnz_max),
+            "pipeline_rank0": ["", "rows", "split", "groups"][st2["pipeline"]]}
     if rank == 0:
         print(json.dumps(line), flush=True)
-    R.close()
     if comm is not None:
         comm.barrier()
         if cleanup:
