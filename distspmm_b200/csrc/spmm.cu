@@ -494,65 +494,71 @@ __global__ void __launch_bounds__(kSpmmThreads, kMinBlocks) spmm_warp_kernel(con
 // exactly (an explicit zero in A counts as present). Lane l holds output columns
 // col0 .. col0 + 3, blockIdx.y selecting a block of 128 columns. Needs N % 128 == 0 and
 // 16-byte aligned B / C rows.
-template <int L>
+template <int RB, int L>
 __device__ __forceinline__ void dia_run(const SpmmArgs &a, const float *sv, int d0, const uint32_t (&pb)[4],
-                                        int64_t jb, int col0, uint64_t pol, float4 (&acc)[kDiaRows]) {
-  constexpr int R = kDiaRows;
+                                        int64_t jb, int col0, uint64_t pol, float4 (&acc)[RB]) {
   using V = Vec<4>;
+  constexpr uint32_t kFull = (1u << RB) - 1u;
   bool all = true;  // every entry of the run is present: no per-entry tests
 #pragma unroll
-  for (int l = 0; l < L; ++l) all = all && pb[l] == 0xffu;
-  float4 b[R + L - 1];
+  for (int l = 0; l < L; ++l) all = all && pb[l] == kFull;
+  float4 b[RB + L - 1];
   if (all) {
 #pragma unroll
-    for (int k = 0; k < R + L - 1; ++k) b[k] = V::ldg(a.B + (jb + k) * a.ldb + col0, pol);
+    for (int k = 0; k < RB + L - 1; ++k) b[k] = V::ldg(a.B + (jb + k) * a.ldb + col0, pol);
 #pragma unroll
-    for (int k = 0; k < R + L - 1; ++k)
+    for (int k = 0; k < RB + L - 1; ++k)
 #pragma unroll
       for (int l = 0; l < L; ++l)
-        if (k - l >= 0 && k - l < R) V::fma(acc[k - l], sv[(d0 + l) * R + k - l], b[k]);
+        if (k - l >= 0 && k - l < RB) V::fma(acc[k - l], sv[(d0 + l) * RB + k - l], b[k]);
     return;
   }
 #pragma unroll
-  for (int k = 0; k < R + L - 1; ++k) {
+  for (int k = 0; k < RB + L - 1; ++k) {
     uint32_t need = 0;  // some present entry of the block uses B row jb + k
 #pragma unroll
     for (int l = 0; l < L; ++l)
-      if (k - l >= 0 && k - l < R) need |= (pb[l] >> (k - l)) & 1u;
+      if (k - l >= 0 && k - l < RB) need |= (pb[l] >> (k - l)) & 1u;
     b[k] = need ? V::ldg(a.B + (jb + k) * a.ldb + col0, pol) : V::zero();
   }
 #pragma unroll
-  for (int k = 0; k < R + L - 1; ++k)
+  for (int k = 0; k < RB + L - 1; ++k)
 #pragma unroll
     for (int l = 0; l < L; ++l)
-      if (k - l >= 0 && k - l < R && ((pb[l] >> (k - l)) & 1u)) V::fma(acc[k - l], sv[(d0 + l) * R + k - l], b[k]);
+      if (k - l >= 0 && k - l < RB && ((pb[l] >> (k - l)) & 1u))
+        V::fma(acc[k - l], sv[(d0 + l) * RB + k - l], b[k]);
 }
 
-template <bool kAccum>
+// RB (4 or 8) consecutive rows per warp; the presence bytes cover 8-row blocks, so a 4-row
+// warp uses half of each byte.
+template <int RB, bool kAccum>
 __global__ void __launch_bounds__(kSpmmThreads) spmm_dia_kernel(const SpmmArgs a) {
-  constexpr int R = kDiaRows;
+  static_assert(RB == 4 || RB == 8, "rows per warp");
   using V = Vec<4>;
-  __shared__ float s_val[kSpmmThreads / 32][kMaxDiag * R];
+  __shared__ float s_val[kSpmmThreads / 32][kMaxDiag * RB];
   const unsigned full = 0xffffffffu;
   const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
-  const int64_t blk = ((int64_t)blockIdx.x * kSpmmThreads + threadIdx.x) >> 5;
-  const int64_t i0 = blk * R;
+  const int64_t wid = ((int64_t)blockIdx.x * kSpmmThreads + threadIdx.x) >> 5;
+  const int64_t i0 = wid * RB;
   if (i0 >= a.dia_m) return;
   const int col0 = blockIdx.y * 128 + lane * 4;
   const int64_t orow0 = a.dia_row0 + i0;
   const uint64_t pol = evict_last_policy();
-  // the block's values, diagonal-major (8 rows each), into this warp's shared slice
+  // this warp's values, diagonal-major (RB rows each), into its shared slice
   float *sv = s_val[wib];
-  for (int idx = lane; idx < a.n_diag * R; idx += 32) {
-    const int d = idx / R, r = idx % R;
+  for (int idx = lane; idx < a.n_diag * RB; idx += 32) {
+    const int d = idx / RB, r = idx % RB;
     sv[idx] = i0 + r < a.dia_m ? __ldg(a.dia_vals + (int64_t)d * a.dia_m + i0 + r) : 0.f;
   }
-  // lane d holds the presence bits of diagonal d for the 8 rows of this block
-  const uint32_t pbyte = lane < a.n_diag ? __ldg(a.dia_pres + blk * a.n_diag + lane) : 0u;
+  // lane d holds the presence bits of diagonal d for the RB rows of this warp
+  const int64_t blk = i0 / kDiaRows;
+  const int shift = (int)(i0 % kDiaRows);
+  const uint32_t pbyte =
+      lane < a.n_diag ? ((uint32_t)__ldg(a.dia_pres + blk * a.n_diag + lane) >> shift) & ((1u << RB) - 1u) : 0u;
   __syncwarp();
-  float4 acc[R];
+  float4 acc[RB];
 #pragma unroll
-  for (int r = 0; r < R; ++r) acc[r] = V::zero();
+  for (int r = 0; r < RB; ++r) acc[r] = V::zero();
 
   int d0 = 0;
   for (int q = 0; q < a.n_runs; ++q) {
@@ -562,15 +568,15 @@ __global__ void __launch_bounds__(kSpmmThreads) spmm_dia_kernel(const SpmmArgs a
     for (int l = 0; l < 4; ++l) pb[l] = __shfl_sync(full, pbyte, min(d0 + l, 31));
     const int64_t jb = orow0 + a.diag_off[d0];  // B row of k = 0
     switch (L) {
-      case 1: dia_run<1>(a, sv, d0, pb, jb, col0, pol, acc); break;
-      case 2: dia_run<2>(a, sv, d0, pb, jb, col0, pol, acc); break;
-      case 3: dia_run<3>(a, sv, d0, pb, jb, col0, pol, acc); break;
-      default: dia_run<4>(a, sv, d0, pb, jb, col0, pol, acc); break;
+      case 1: dia_run<RB, 1>(a, sv, d0, pb, jb, col0, pol, acc); break;
+      case 2: dia_run<RB, 2>(a, sv, d0, pb, jb, col0, pol, acc); break;
+      case 3: dia_run<RB, 3>(a, sv, d0, pb, jb, col0, pol, acc); break;
+      default: dia_run<RB, 4>(a, sv, d0, pb, jb, col0, pol, acc); break;
     }
     d0 += L;
   }
 #pragma unroll
-  for (int r = 0; r < R; ++r) {
+  for (int r = 0; r < RB; ++r) {
     if (i0 + r >= a.dia_m) break;
     const int32_t row = (int32_t)(orow0 + r);
     float *dst = a.C + (int64_t)row * a.ldc + col0;
@@ -820,10 +826,15 @@ int launch_spmm(const SpmmArgs &a, bool accumulate, cudaStream_t stream) {
   const bool dia = env_dia && a.variant == kRowSplit && a.dia_vals && a.dia_m > 0 && a.N % 128 == 0 &&
                    a.ldb % 4 == 0 && a.ldc % 4 == 0 && aligned(a.B, 16) && aligned(a.C, 16);
   if (dia) {
-    const int64_t blocks = (a.dia_m + kDiaRows - 1) / kDiaRows;
-    const int64_t gx = (blocks + kSpmmThreads / 32 - 1) / (kSpmmThreads / 32);
-    if (gx > INT32_MAX) return fail(DSP_ERR_UNSUPPORTED, "spmm: %lld row blocks", (long long)blocks);
-    KernelFn k = accumulate ? spmm_dia_kernel<true> : spmm_dia_kernel<false>;
+    // rows per warp: 8 (each B row of a run serves up to 8 rows) or 4 (half the registers,
+    // twice the warps); DSP_SPMM_DIA_ROWS picks
+    const char *env_rows = getenv("DSP_SPMM_DIA_ROWS");  // read per launch (tests switch it)
+    const int rb = env_rows && atoi(env_rows) == 4 ? 4 : 8;
+    const int64_t warps = (a.dia_m + rb - 1) / rb;
+    const int64_t gx = (warps + kSpmmThreads / 32 - 1) / (kSpmmThreads / 32);
+    if (gx > INT32_MAX) return fail(DSP_ERR_UNSUPPORTED, "spmm: %lld row blocks", (long long)warps);
+    KernelFn k = rb == 4 ? (accumulate ? spmm_dia_kernel<4, true> : spmm_dia_kernel<4, false>)
+                         : (accumulate ? spmm_dia_kernel<8, true> : spmm_dia_kernel<8, false>);
     k<<<dim3((unsigned)gx, (unsigned)(a.N / 128)), kSpmmThreads, 0, stream>>>(a);
   } else if (units > 0 && ws.VPL > 0) {
     KernelFn k = warp_kernel_for(ws.VPL, ws.U, accumulate, ws.MB);

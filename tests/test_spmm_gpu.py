@@ -218,12 +218,14 @@ def _banded(m, offsets, keep, seed):
     return d.Csr(np.array(ip, np.int64), np.array(ix, np.int64), vals, m, m)
 
 
-def test_banded_diagonal_kernel_absent_entries_read_nothing(gpu):
-    """Banded operands run on the diagonal kernel. An entry that does not exist must not
-    read B: B rows that no entry uses hold NaN, and C must stay finite and match the
-    oracle. Rows near the matrix edges, rows without entries, and row counts that are not
-    a multiple of the 8-row blocks are included."""
+@pytest.mark.parametrize("rows_per_warp", ["8", "4"])
+def test_banded_diagonal_kernel_absent_entries_read_nothing(gpu, monkeypatch, rows_per_warp):
+    """Banded operands run on the diagonal kernel (8 or 4 rows per warp). An entry that does
+    not exist must not read B: B rows that no entry uses hold NaN, and C must stay finite and
+    match the oracle. Rows near the matrix edges, rows without entries, and row counts that
+    are not a multiple of the 8-row blocks are included."""
     import torch
+    monkeypatch.setenv("DSP_SPMM_DIA_ROWS", rows_per_warp)
     from distspmm_b200.spmm import SpmmPlan
     m, N = 1003, 128
     # offsets -2..2 (one run) and +-100 (single diagonals); column 500 and 777 are never used
@@ -247,10 +249,12 @@ def test_banded_diagonal_kernel_absent_entries_read_nothing(gpu):
     assert ok, worst
 
 
-def test_banded_explicit_zero_still_reads_its_b_row(gpu):
+@pytest.mark.parametrize("rows_per_warp", ["8", "4"])
+def test_banded_explicit_zero_still_reads_its_b_row(gpu, monkeypatch, rows_per_warp):
     """An explicit 0.0 in A is an entry: its B row is read, so a NaN there gives NaN in C,
     exactly as the CSR product (and the oracle) gives."""
     import torch
+    monkeypatch.setenv("DSP_SPMM_DIA_ROWS", rows_per_warp)
     from distspmm_b200.spmm import SpmmPlan
     m, N = 64, 128
     A = _banded(m, [-1, 0, 1], lambda i, o: True, seed=4)
@@ -264,9 +268,11 @@ def test_banded_explicit_zero_still_reads_its_b_row(gpu):
     assert nan_rows == [10, 11, 12]  # every row with an entry in column 11, the zero included
 
 
-def test_stencil_diagonal_kernel_widths(gpu):
+@pytest.mark.parametrize("rows_per_warp", ["8", "4"])
+def test_stencil_diagonal_kernel_widths(gpu, monkeypatch, rows_per_warp):
     """The 27-point stencil (the banded benchmark matrix) at several widths: N = 128 and 256
     use the diagonal kernel, N = 64 and 100 the row kernels; all match the oracle."""
+    monkeypatch.setenv("DSP_SPMM_DIA_ROWS", rows_per_warp)
     A = d.gen_stencil27(14, seed=7)
     for N in (64, 100, 128, 256):
         B, C, plan = _run(A, N)
