@@ -121,6 +121,7 @@ PROTOTYPES = {
     "dsp_spmm_plan_destroy": (None, [c_vp]),
     "dsp_spmm_plan_info": (c_int, [c_vp, P(dsp_spmm_info)]),
     "dsp_spmm_f32": (c_int, [c_vp, c_vp, c_i64, c_vp, c_i64, c_int, c_int, c_vp]),
+    "dsp_spmm_check_error": (c_int, [c_vp]),
     "dsp_spmm_csr_f32_noalloc": (c_int, [c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_vp, c_i64, c_int,
                                          c_int, c_vp]),
     "dsp_rank_create": (c_int, [P(dsp_rank_desc), P(c_vp)]),

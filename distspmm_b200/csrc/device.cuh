@@ -41,6 +41,7 @@ struct SpmmArgs {
   const float *vals;    // [nnz]
   const float *B;
   int64_t ldb;
+  int64_t b_rows;  // rows of B (the operand's columns); 0 = unknown
   float *C;
   int64_t ldc;
   float *partial;  // [slots][N]
@@ -58,6 +59,7 @@ struct SpmmArgs {
   int32_t diag_off[kMaxDiag];   // ascending
   int n_runs;                    // runs of consecutive offsets (o, o+1, ..., at most 4 long)
   uint8_t run_len[kMaxDiag];     // in offset order
+  int *err;  // device error word set by a kernel whose bounded wait gave up (nullptr: none)
 };
 
 struct SpmmShape {

@@ -26,6 +26,7 @@
 
 #include "device.cuh"
 #include "internal.h"
+#include "mbar.cuh"
 
 namespace dsp {
 
@@ -33,29 +34,7 @@ namespace {
 
 constexpr int kStages = 8;
 constexpr int kStageBytes = 16384;
-constexpr long long kWaitCycles = 4000000000ll;  // ~2 s at B200 clocks
-
-__device__ __forceinline__ uint32_t smem_addr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
-
-// Bounded wait for phase `parity` of an mbarrier; false (and *err set) after `budget`
-// clock64 cycles.
-__device__ __forceinline__ bool mbar_wait(uint32_t mbar, uint32_t parity, int *err, int code,
-                                          long long budget = kWaitCycles) {
-  const long long t0 = clock64();
-  while (true) {
-    uint32_t done;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
-        : "=r"(done)
-        : "r"(mbar), "r"(parity)
-        : "memory");
-    if (done) return true;
-    if (clock64() - t0 > budget) {
-      atomicExch(err, code);
-      return false;
-    }
-  }
-}
+constexpr long long kWaitCycles = kMbarWaitCycles;
 
 // Self-test of the bounded wait: an mbarrier that nothing arrives at (a flag nothing sets).
 __global__ void bounded_wait_selftest_kernel(long long budget, int *err) {

@@ -767,6 +767,7 @@ int step_groups(dsp_rank *r, cudaStream_t stream) {
     if (op.units() == 0) continue;
     DSP_CUDA(cudaEventRecord(r->ev_seg_begin[(size_t)k], r->compute));
     SpmmArgs sa = op.args(r->B, r->dims, r->C, r->dims, r->dims, r->scratch);
+    sa.err = r->d_err;
     sa.first_phase = r->d_first_phase;  // rows written by segment 0 are accumulated
     sa.phase = k;
     if ((rc = launch_spmm(sa, false, r->compute))) return rc;
@@ -833,6 +834,7 @@ extern "C" int dsp_rank_step(dsp_rank *r, void *stream_v) {
       if (has_fetch[(size_t)waited + 1]) DSP_CUDA(cudaStreamWaitEvent(r->compute, r->ev_fetch[(size_t)waited + 1], 0));
     DSP_CUDA(cudaEventRecord(r->ev_seg_begin[(size_t)k], r->compute));
     SpmmArgs sa = op.args(r->B, r->dims, r->C, r->dims, r->dims, r->scratch);
+    sa.err = r->d_err;
     if (r->pipeline == DSP_PIPELINE_SPLIT) {  // rows written by an earlier phase are accumulated
       sa.first_phase = r->d_first_phase;
       sa.phase = k;

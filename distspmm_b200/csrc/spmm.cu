@@ -22,6 +22,7 @@
 // read-only path with an L2 evict_last policy (A and C stream past them); final C rows
 // are written once with streaming stores.
 // Replaces cusparseSpMM(COO, ALG_DEFAULT, beta = 1) of src/dist_spmm_node.cu:354-385.
+#include <cuda.h>  // CUtensorMap and its enums (the encoder is fetched through the runtime)
 #include <cuda_runtime.h>
 #include <stdlib.h>
 #include <string.h>
@@ -30,6 +31,7 @@
 
 #include "device.cuh"
 #include "internal.h"
+#include "mbar.cuh"
 
 namespace dsp {
 
@@ -586,6 +588,182 @@ __global__ void __launch_bounds__(kSpmmThreads) spmm_dia_kernel(const SpmmArgs a
   }
 }
 
+// ------------------------------------------------------------------ diagonal kernel, TMA-staged B
+//
+// The banded kernel with its B rows staged in shared memory by the tensor-memory
+// accelerator. Persistent CTAs (MB per SM) of W consumer warps and one producer warp (W + 1
+// a multiple of 4: whole warps per scheduler). A work item is R = 8W consecutive listed
+// rows x 128 columns. For each run of consecutive offsets
+// [o, o + L) the item's rows need B rows [row0 + o, row0 + o + R + L - 1); the producer
+// loads that window (a box of R + 3 rows x 128 columns; rows outside B are zero-filled, and
+// no present entry uses them) with one cp.async.bulk.tensor.2d into an S-stage ring, its
+// completion counted in bytes on the stage's mbarrier. A consumer warp reads its 8 + L - 1
+// rows of the window from shared memory once each and applies each to the up to L of its 8
+// rows that use it, so a B element crosses L2 -> SM once per run (9 times per output row of
+// a 27-point stencil) and no warp waits on a global load in the inner loop. Values and
+// presence bits of the next item are loaded into registers during the current one.
+// Every mbarrier wait is bounded: on timeout the kernel records a code in *a.err, the
+// producer waits (bounded) for the windows it issued, and the CTA returns.
+template <int W>
+struct DiaTmaShape {
+  static constexpr int kRows = 8 * W;              // rows per item
+  static constexpr int kBoxRows = kRows + 3;       // window rows (runs are at most 4 long)
+  static constexpr int kStageBytes = kBoxRows * 128 * 4;
+  static constexpr int kThreads = 32 * (W + 1);
+  static constexpr int kValBytes = W * kMaxDiag * 8 * 4;  // per warp: [diag][8 rows]
+};
+
+template <int L, bool kAll>
+__device__ __forceinline__ void dia_tma_run(const float *wrow, const float *sv, int d0, const uint32_t (&pb)[4],
+                                            float4 (&acc)[8]) {
+  using V = Vec<4>;
+  float v[L][8];
+#pragma unroll
+  for (int l = 0; l < L; ++l) {
+    const float4 lo = *reinterpret_cast<const float4 *>(sv + (d0 + l) * 8);
+    const float4 hi = *reinterpret_cast<const float4 *>(sv + (d0 + l) * 8 + 4);
+    v[l][0] = lo.x, v[l][1] = lo.y, v[l][2] = lo.z, v[l][3] = lo.w;
+    v[l][4] = hi.x, v[l][5] = hi.y, v[l][6] = hi.z, v[l][7] = hi.w;
+  }
+#pragma unroll
+  for (int k = 0; k < 8 + L - 1; ++k) {
+    const float4 b = *reinterpret_cast<const float4 *>(wrow + k * 128);
+#pragma unroll
+    for (int l = 0; l < L; ++l) {
+      const int r = k - l;
+      if (r >= 0 && r < 8 && (kAll || ((pb[l] >> r) & 1u))) V::fma(acc[r], v[l][r], b);
+    }
+  }
+}
+
+template <int W, int S, int MB, bool kAccum>
+__global__ void __launch_bounds__(32 * (W + 1), MB)
+    spmm_dia_tma_kernel(const SpmmArgs a, const __grid_constant__ CUtensorMap tmap) {
+  using V = Vec<4>;
+  using D = DiaTmaShape<W>;
+  extern __shared__ __align__(1024) unsigned char dsm[];
+  __shared__ __align__(8) uint64_t full_bar[S], empty_bar[S];
+  float *win = reinterpret_cast<float *>(dsm);  // [S][kBoxRows][128]
+  const unsigned all = 0xffffffffu;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int ncb = a.N / 128;
+  const int64_t items = (a.dia_m + D::kRows - 1) / D::kRows * ncb;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(smem_addr(&full_bar[s]), 1);
+      mbar_init(smem_addr(&empty_bar[s]), W);
+    }
+    mbar_fence_init();
+  }
+  __syncthreads();
+
+  if (warp == W) {  // producer: one thread issues every window of this CTA's items
+    if (lane != 0) return;
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tmap) : "memory");
+    int64_t use = 0;
+    bool ok = true;
+    for (int64_t t = blockIdx.x; t < items && ok; t += gridDim.x) {
+      const int64_t row0 = a.dia_row0 + t / ncb * D::kRows;
+      const int32_t x = (int32_t)(t % ncb) * 128;
+      int d0 = 0;
+      for (int q = 0; q < a.n_runs; ++q) {
+        const int s = (int)(use % S);
+        const int64_t j = use / S;
+        if (j > 0 && !mbar_wait(smem_addr(&empty_bar[s]), (uint32_t)((j - 1) & 1), a.err, 5)) {
+          ok = false;
+          break;
+        }
+        const uint32_t fb = smem_addr(&full_bar[s]);
+        mbar_arrive_expect_tx(fb, D::kStageBytes);
+        const int32_t y = (int32_t)(row0 + a.diag_off[d0]);
+        asm volatile(
+            "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+            "[%4];" ::"r"(smem_addr(win + (size_t)s * D::kBoxRows * 128)),
+            "l"(&tmap), "r"(x), "r"(y), "r"(fb)
+            : "memory");
+        ++use;
+        d0 += a.run_len[q];
+      }
+    }
+    // every issued window has landed before the CTA's shared memory goes away
+    for (int64_t u = use > S ? use - S : 0; u < use; ++u)
+      if (!mbar_wait(smem_addr(&full_bar[u % S]), (uint32_t)((u / S) & 1), a.err, 6)) break;
+    return;
+  }
+
+  // consumers
+  float *sv = reinterpret_cast<float *>(dsm + (size_t)S * D::kStageBytes) + warp * (kMaxDiag * 8);
+  const int col = lane * 4;
+  const int nv = a.n_diag * 8;  // values per warp and item, <= 256: 8 per lane
+  float pv[8];
+  uint32_t ppb = 0;
+  auto prefetch = [&](int64_t t) {
+    const int64_t i0 = t / ncb * D::kRows + warp * 8;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int idx = lane + 32 * k, d = idx >> 3, r = idx & 7;
+      pv[k] = t < items && idx < nv && i0 + r < a.dia_m ? __ldg(a.dia_vals + (int64_t)d * a.dia_m + i0 + r) : 0.f;
+    }
+    ppb = t < items && lane < a.n_diag && i0 < a.dia_m ? __ldg(a.dia_pres + i0 / kDiaRows * a.n_diag + lane) : 0u;
+  };
+  prefetch(blockIdx.x);
+  int64_t use = 0;
+  for (int64_t t = blockIdx.x; t < items; t += gridDim.x) {
+    const int64_t i0 = t / ncb * D::kRows + warp * 8;
+    const int cb = (int)(t % ncb);
+    __syncwarp();  // the previous item's reads of sv are done
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      if (lane + 32 * k < nv) sv[lane + 32 * k] = pv[k];
+    const uint32_t pbyte = ppb;
+    const uint32_t fullmask = __ballot_sync(all, pbyte == 0xffu);
+    __syncwarp();
+    prefetch(t + gridDim.x);
+    float4 acc[8];
+#pragma unroll
+    for (int r = 0; r < 8; ++r) acc[r] = V::zero();
+    int d0 = 0;
+    for (int q = 0; q < a.n_runs; ++q) {
+      const int L = a.run_len[q];
+      const int s = (int)(use % S);
+      if (!mbar_wait(smem_addr(&full_bar[s]), (uint32_t)((use / S) & 1), a.err, 7)) return;
+      const float *wrow = win + ((size_t)s * D::kBoxRows + warp * 8) * 128 + col;
+      const uint32_t lmask = (1u << L) - 1u;
+      uint32_t pb[4] = {0u, 0u, 0u, 0u};
+      if (((fullmask >> d0) & lmask) == lmask) {
+        switch (L) {
+          case 1: dia_tma_run<1, true>(wrow, sv, d0, pb, acc); break;
+          case 2: dia_tma_run<2, true>(wrow, sv, d0, pb, acc); break;
+          case 3: dia_tma_run<3, true>(wrow, sv, d0, pb, acc); break;
+          default: dia_tma_run<4, true>(wrow, sv, d0, pb, acc); break;
+        }
+      } else {
+#pragma unroll
+        for (int l = 0; l < 4; ++l) pb[l] = __shfl_sync(all, pbyte, min(d0 + l, 31));
+        switch (L) {
+          case 1: dia_tma_run<1, false>(wrow, sv, d0, pb, acc); break;
+          case 2: dia_tma_run<2, false>(wrow, sv, d0, pb, acc); break;
+          case 3: dia_tma_run<3, false>(wrow, sv, d0, pb, acc); break;
+          default: dia_tma_run<4, false>(wrow, sv, d0, pb, acc); break;
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_addr(&empty_bar[s]));
+      ++use;
+      d0 += L;
+    }
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      if (i0 + r >= a.dia_m) break;
+      const int32_t row = (int32_t)(a.dia_row0 + i0 + r);
+      float *dst = a.C + (int64_t)row * a.ldc + cb * 128 + col;
+      float4 out = acc[r];
+      if (accumulates<kAccum>(a, row)) V::add(out, V::ld(dst));
+      V::st_stream(dst, out);
+    }
+  }
+}
+
 // ------------------------------------------------------------------ fixup and fills
 
 // One warp per cut row: C[row] = (accumulating ? C[row] : 0) + sum of its partial slots,
@@ -811,6 +989,78 @@ SpmmShape spmm_shape(int N, int variant, const float *B, int64_t ldb, const floa
   return s;
 }
 
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link against libcuda)
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess) {
+      cudaGetLastError();
+      return (EncodeTiledFn) nullptr;
+    }
+    return (EncodeTiledFn)p;
+  }();
+  return fn;
+}
+
+// The TMA-staged diagonal kernel for a banded launch; DSP_ERR_UNSUPPORTED (nothing launched)
+// when it does not apply: DSP_SPMM_DIA_TMA=0, no error word, or a B the tensor map cannot
+// describe. DSP_SPMM_DIA_TMA_SHAPE picks the CTA shape: 1 = two CTAs per SM of 7 consumer
+// warps with 3 stages each (the default), 2 = one CTA of 15 consumer warps with 3 stages.
+struct DiaTmaLaunch {
+  void (*k)(const SpmmArgs, const CUtensorMap);
+  int W, S, MB;
+};
+
+template <int W, int S, int MB>
+DiaTmaLaunch dia_tma_launch(bool accumulate) {
+  return {accumulate ? spmm_dia_tma_kernel<W, S, MB, true> : spmm_dia_tma_kernel<W, S, MB, false>, W, S, MB};
+}
+
+int launch_dia_tma(const SpmmArgs &a, bool accumulate, cudaStream_t stream) {
+  const char *env = getenv("DSP_SPMM_DIA_TMA");  // read per launch (tests switch it)
+  if ((env && atoi(env) == 0) || !a.err || a.b_rows <= 0 || a.b_rows > INT32_MAX || a.ldb % 4 != 0 ||
+      !aligned(a.B, 16))
+    return DSP_ERR_UNSUPPORTED;
+  EncodeTiledFn encode = encode_tiled();
+  if (!encode) return DSP_ERR_UNSUPPORTED;
+  const char *env_shape = getenv("DSP_SPMM_DIA_TMA_SHAPE");
+  const DiaTmaLaunch L = env_shape && atoi(env_shape) == 2 ? dia_tma_launch<15, 3, 1>(accumulate)
+                                                           : dia_tma_launch<7, 3, 2>(accumulate);
+  const int rows_per_item = 8 * L.W, box_rows = rows_per_item + 3;
+  const size_t smem = (size_t)L.S * box_rows * 128 * sizeof(float) + (size_t)L.W * kMaxDiag * 8 * sizeof(float);
+  CUtensorMap tmap;
+  const cuuint64_t gdim[2] = {(cuuint64_t)a.N, (cuuint64_t)a.b_rows};
+  const cuuint64_t gstride[1] = {(cuuint64_t)a.ldb * sizeof(float)};
+  const cuuint32_t box[2] = {128, (cuuint32_t)box_rows};
+  const cuuint32_t estride[2] = {1, 1};
+  if (encode(&tmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void *)a.B, gdim, gstride, box, estride,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return DSP_ERR_UNSUPPORTED;
+  int device = 0, sms = 0;
+  cudaGetDevice(&device);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  // all of the unified L1 / shared array as shared memory, so MB CTAs fit on an SM
+  if (cudaFuncSetAttribute((const void *)L.k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+          cudaSuccess ||
+      cudaFuncSetAttribute((const void *)L.k, cudaFuncAttributePreferredSharedMemoryCarveout,
+                           (int)cudaSharedmemCarveoutMaxShared) != cudaSuccess) {
+    cudaGetLastError();
+    return DSP_ERR_UNSUPPORTED;
+  }
+  const int64_t items = (a.dia_m + rows_per_item - 1) / rows_per_item * (a.N / 128);
+  const int64_t grid = std::min<int64_t>(items, (int64_t)std::max(sms, 1) * L.MB);
+  L.k<<<(unsigned)grid, 32 * (L.W + 1), smem, stream>>>(a, tmap);
+  return DSP_OK;
+}
+
 int launch_spmm(const SpmmArgs &a, bool accumulate, cudaStream_t stream) {
   if (a.N <= 0) return DSP_OK;
   const SpmmShape s = spmm_shape(a.N, a.variant, a.B, a.ldb, a.C, a.ldc);
@@ -825,7 +1075,9 @@ int launch_spmm(const SpmmArgs &a, bool accumulate, cudaStream_t stream) {
   }();
   const bool dia = env_dia && a.variant == kRowSplit && a.dia_vals && a.dia_m > 0 && a.N % 128 == 0 &&
                    a.ldb % 4 == 0 && a.ldc % 4 == 0 && aligned(a.B, 16) && aligned(a.C, 16);
-  if (dia) {
+  if (dia && launch_dia_tma(a, accumulate, stream) == DSP_OK) {
+    // launched: the TMA-staged diagonal kernel
+  } else if (dia) {
     // rows per warp: 8 (each B row of a run serves up to 8 rows) or 4 (half the registers,
     // twice the warps); DSP_SPMM_DIA_ROWS picks
     const char *env_rows = getenv("DSP_SPMM_DIA_ROWS");  // read per launch (tests switch it)
@@ -1169,6 +1421,7 @@ SpmmArgs DevOperand::args(const float *B, int64_t ldb, float *C, int64_t ldc, in
   a.vals = d_vals;
   a.B = B;
   a.ldb = ldb;
+  a.b_rows = cols;
   a.C = C;
   a.ldc = ldc;
   a.partial = partial;
@@ -1218,6 +1471,7 @@ struct dsp_spmm_plan {
   dsp::DevOperand op;
   float *scratch = nullptr;
   int64_t scratch_floats = 0;
+  int *d_err = nullptr;  // set by a kernel whose bounded wait gave up (dsp_spmm_check_error)
 };
 
 using namespace dsp;
@@ -1248,6 +1502,9 @@ extern "C" int dsp_spmm_plan_create(int device, const dsp_csr *a, int dims_hint,
     e = cudaMalloc(&p->scratch, sizeof(float) * (size_t)p->scratch_floats);
     if (e != cudaSuccess) rc = fail(DSP_ERR_NOMEM, "spmm scratch: %s", cudaGetErrorString(e));
   }
+  if (rc == DSP_OK && ((e = cudaMalloc(&p->d_err, sizeof(int))) != cudaSuccess ||
+                       (e = cudaMemset(p->d_err, 0, sizeof(int))) != cudaSuccess))
+    rc = fail(DSP_ERR_NOMEM, "spmm error word: %s", cudaGetErrorString(e));
   if (rc) {
     dsp_spmm_plan_destroy(p);
     return rc;
@@ -1261,7 +1518,19 @@ extern "C" void dsp_spmm_plan_destroy(dsp_spmm_plan *p) {
   cudaSetDevice(p->op.device);
   p->op.release();
   if (p->scratch) cudaFree(p->scratch);
+  if (p->d_err) cudaFree(p->d_err);
   delete p;
+}
+
+extern "C" int dsp_spmm_check_error(dsp_spmm_plan *p) {
+  DSP_TRY_ARG(p, "dsp_spmm_check_error: null plan");
+  cudaError_t e = cudaSetDevice(p->op.device);
+  int flag = 0;
+  if (e == cudaSuccess) e = cudaMemcpy(&flag, p->d_err, sizeof flag, cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess && flag != 0) e = cudaMemset(p->d_err, 0, sizeof(int));
+  if (e != cudaSuccess) return fail(DSP_ERR_CUDA, "dsp_spmm_check_error: %s", cudaGetErrorString(e));
+  if (flag == 0) return DSP_OK;
+  return fail(DSP_ERR_TIMEOUT, "spmm: a bounded wait gave up (code %d); C is incomplete", flag);
 }
 
 extern "C" int dsp_spmm_plan_info(const dsp_spmm_plan *p, dsp_spmm_info *info) {
@@ -1301,6 +1570,7 @@ extern "C" int dsp_spmm_f32(dsp_spmm_plan *p, const float *B, int64_t ldb, float
     }
   }
   SpmmArgs a = p->op.args(B, ldb, C, ldc, N, p->scratch);
+  a.err = p->d_err;
   return launch_spmm(a, accumulate != 0, (cudaStream_t)stream);
 }
 

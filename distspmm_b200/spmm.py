@@ -49,6 +49,11 @@ class SpmmPlan:
         self.run_ptr(B.data_ptr(), B.stride(0), C.data_ptr(), C.stride(0), N, accumulate, stream)
         return C
 
+    def check_error(self) -> None:
+        """After the stream was synchronised: raise DspError if a kernel's bounded wait on its
+        staged copies gave up (the flag is cleared)."""
+        call("dsp_spmm_check_error", self._h)
+
     def close(self) -> None:
         if getattr(self, "_h", None):
             lib().dsp_spmm_plan_destroy(self._h)

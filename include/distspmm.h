@@ -263,6 +263,11 @@ int dsp_spmm_plan_info(const dsp_spmm_plan *p, dsp_spmm_info *info);
  * ldc. Enqueued on `stream`; returns immediately. */
 int dsp_spmm_f32(dsp_spmm_plan *p, const float *B, int64_t ldb, float *C, int64_t ldc, int N,
                  int accumulate, void *stream);
+/* After the stream of earlier dsp_spmm_f32 calls was synchronised: DSP_OK, or
+ * DSP_ERR_TIMEOUT if a kernel's bounded wait on its shared-memory copies gave up (the
+ * banded kernel's staged windows); the flag is cleared. Not in the reference (no failure
+ * detection there, src/utils.h:26-84). */
+int dsp_spmm_check_error(dsp_spmm_plan *p);
 
 /* Allocation-free SpMM (no counterpart in the reference). C = A*B (accumulate = 0) or
  * C += A*B on the current CUDA device, for a CSR matrix the caller already holds in device
@@ -396,7 +401,8 @@ int dsp_rank_upload_b_owned(dsp_rank *r, const float *B_owned_host, void *stream
  * step's B before the call (the caller's barrier). */
 int dsp_rank_step(dsp_rank *r, void *stream);
 /* After the step's stream was synchronised: DSP_OK, or DSP_ERR_TIMEOUT if a fetch kernel's
- * bounded wait on its bulk copies gave up during an earlier step (the flag is cleared).
+ * or the banded SpMM kernel's bounded wait on its bulk copies gave up during an earlier
+ * step (the flag is cleared).
  * The reference has no failure detection (src/utils.h:26-84 exit() on any error). */
 int dsp_rank_check_error(dsp_rank *r);
 /* Test of the fetch kernels' bounded wait on the current device: one CTA waits on an

@@ -218,14 +218,29 @@ def _banded(m, offsets, keep, seed):
     return d.Csr(np.array(ip, np.int64), np.array(ix, np.int64), vals, m, m)
 
 
-@pytest.mark.parametrize("rows_per_warp", ["8", "4"])
-def test_banded_diagonal_kernel_absent_entries_read_nothing(gpu, monkeypatch, rows_per_warp):
-    """Banded operands run on the diagonal kernel (8 or 4 rows per warp). An entry that does
+# the diagonal kernel's configurations: TMA-staged windows (two CTA shapes) and the register
+# kernel (8 or 4 rows per warp)
+DIA_KERNELS = {
+    "tma_7x2": {"DSP_SPMM_DIA_TMA": "1", "DSP_SPMM_DIA_TMA_SHAPE": "1"},
+    "tma_15": {"DSP_SPMM_DIA_TMA": "1", "DSP_SPMM_DIA_TMA_SHAPE": "2"},
+    "reg_8": {"DSP_SPMM_DIA_TMA": "0", "DSP_SPMM_DIA_ROWS": "8"},
+    "reg_4": {"DSP_SPMM_DIA_TMA": "0", "DSP_SPMM_DIA_ROWS": "4"},
+}
+
+
+def _dia_kernel(monkeypatch, name):
+    for k, v in DIA_KERNELS[name].items():
+        monkeypatch.setenv(k, v)
+
+
+@pytest.mark.parametrize("kernel", list(DIA_KERNELS))
+def test_banded_diagonal_kernel_absent_entries_read_nothing(gpu, monkeypatch, kernel):
+    """Banded operands run on the diagonal kernel (each configuration). An entry that does
     not exist must not read B: B rows that no entry uses hold NaN, and C must stay finite and
-    match the oracle. Rows near the matrix edges, rows without entries, and row counts that
-    are not a multiple of the 8-row blocks are included."""
+    match the oracle. Rows near the matrix edges (windows reaching outside B), rows without
+    entries, and row counts that are not a multiple of the 8-row blocks are included."""
     import torch
-    monkeypatch.setenv("DSP_SPMM_DIA_ROWS", rows_per_warp)
+    _dia_kernel(monkeypatch, kernel)
     from distspmm_b200.spmm import SpmmPlan
     m, N = 1003, 128
     # offsets -2..2 (one run) and +-100 (single diagonals); column 500 and 777 are never used
@@ -247,14 +262,15 @@ def test_banded_diagonal_kernel_absent_entries_read_nothing(gpu, monkeypatch, ro
     C2 = plan(torch.from_numpy(B).cuda(), torch.from_numpy(C0.copy()).cuda(), accumulate=True).cpu().numpy()
     ok, worst = oracle.check_close(C2, ref + C0, ab + np.abs(C0), RTOL)
     assert ok, worst
+    plan.check_error()
 
 
-@pytest.mark.parametrize("rows_per_warp", ["8", "4"])
-def test_banded_explicit_zero_still_reads_its_b_row(gpu, monkeypatch, rows_per_warp):
+@pytest.mark.parametrize("kernel", list(DIA_KERNELS))
+def test_banded_explicit_zero_still_reads_its_b_row(gpu, monkeypatch, kernel):
     """An explicit 0.0 in A is an entry: its B row is read, so a NaN there gives NaN in C,
     exactly as the CSR product (and the oracle) gives."""
     import torch
-    monkeypatch.setenv("DSP_SPMM_DIA_ROWS", rows_per_warp)
+    _dia_kernel(monkeypatch, kernel)
     from distspmm_b200.spmm import SpmmPlan
     m, N = 64, 128
     A = _banded(m, [-1, 0, 1], lambda i, o: True, seed=4)
@@ -268,12 +284,39 @@ def test_banded_explicit_zero_still_reads_its_b_row(gpu, monkeypatch, rows_per_w
     assert nan_rows == [10, 11, 12]  # every row with an entry in column 11, the zero included
 
 
-@pytest.mark.parametrize("rows_per_warp", ["8", "4"])
-def test_stencil_diagonal_kernel_widths(gpu, monkeypatch, rows_per_warp):
+@pytest.mark.parametrize("kernel", list(DIA_KERNELS))
+def test_stencil_diagonal_kernel_widths(gpu, monkeypatch, kernel):
     """The 27-point stencil (the banded benchmark matrix) at several widths: N = 128 and 256
     use the diagonal kernel, N = 64 and 100 the row kernels; all match the oracle."""
-    monkeypatch.setenv("DSP_SPMM_DIA_ROWS", rows_per_warp)
+    _dia_kernel(monkeypatch, kernel)
     A = d.gen_stencil27(14, seed=7)
     for N in (64, 100, 128, 256):
         B, C, plan = _run(A, N)
         _check(A, B, C)
+        plan.check_error()
+
+
+@pytest.mark.parametrize("kernel", ["tma_7x2", "tma_15"])
+def test_banded_tma_windows_many_items_per_cta(gpu, monkeypatch, kernel):
+    """Enough rows that every persistent CTA of the TMA-staged kernel takes many items, so
+    its stage ring wraps many times (bounded waits on both barriers of every stage); holes
+    in the band take the per-entry path. Results match the oracle and are bit-identical
+    across runs."""
+    import torch
+    from distspmm_b200.spmm import SpmmPlan
+    _dia_kernel(monkeypatch, kernel)
+    m, N = 150_001, 256
+    rng = np.random.default_rng(11)
+    holes = rng.random((m, 7)) < 0.02
+    offs = [-300, -2, -1, 0, 1, 2, 300]
+    A = _banded(m, offs, lambda i, o: not holes[i, offs.index(o)], seed=12)
+    B = d.dense_b(m, N, 13)
+    plan = SpmmPlan(A, 0, N)
+    assert plan.info()["variant"] == 0
+    Bt = torch.from_numpy(B).cuda()
+    C1 = plan(Bt)
+    C2 = plan(Bt)
+    torch.cuda.synchronize()
+    plan.check_error()
+    assert torch.equal(C1, C2)
+    _check(A, B, C1.cpu().numpy())
