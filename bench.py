@@ -82,6 +82,8 @@ def parse_args(argv=None):
     ap.add_argument("--platform", choices=["h100", "a800", "b200"], default="b200",
                     help="adaptive selector constants (comm_type 2); b200 = the NVLink 5 fit of comm_test")
     ap.add_argument("--seed", type=int, default=1)
+    ap.add_argument("--csr-cache", default=None,
+                    help="directory that keeps generated matrices (binary CSR) for later runs")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-flush", action="store_true")
@@ -119,6 +121,15 @@ def workload_name(a):
     if a.matrix == "uniform":
         return f"uniform{a.rows}x{a.nnz_per_row}_n{a.dims}"
     return f"rmat{a.scale}_n{a.dims}"
+
+
+def matrix_key(a):
+    """File-name key of the generated matrix (everything that determines it)."""
+    if a.matrix == "stencil27":
+        return f"stencil{a.grid}_s{a.seed}"
+    if a.matrix == "uniform":
+        return f"uniform{a.rows}x{a.nnz_per_row}_s{a.seed}"
+    return f"rmat{a.scale}_s{a.seed}"
 
 
 def matrix_desc(a):
@@ -334,17 +345,48 @@ def load_local(a, rank, world, comm):
 
     import distspmm_b200 as d
     from distspmm_b200 import planner
-    if world == 1:
+    # --csr-cache DIR: the generated matrix is kept in DIR/<matrix key> (reference binary CSR
+    # files) and read back by later runs with the same matrix arguments
+    key = os.path.join(a.csr_cache, f"{matrix_key(a)}") if a.csr_cache else None
+    cached = key is not None and os.path.exists(os.path.join(key, "A_indptr.bin"))
+
+    def generate_into(dirpath):
         A = make_workload(a)
+        tmpd = tempfile.mkdtemp(prefix=".dsp_tmp_", dir=os.path.dirname(dirpath))
+        d.save_csr(os.path.join(tmpd, "A"), A)
+        try:
+            os.rename(tmpd, dirpath)
+        except OSError:  # another run stored it first
+            for f in os.listdir(tmpd):
+                os.unlink(os.path.join(tmpd, f))
+            os.rmdir(tmpd)
+        return A
+
+    if world == 1:
+        if cached:
+            ip = np.fromfile(os.path.join(key, "A_indptr.bin"), np.int64)
+            A = d.load_rows(os.path.join(key, "A"), 0, ip.size - 1)
+        elif key is not None:
+            os.makedirs(a.csr_cache, exist_ok=True)
+            A = generate_into(key)
+        else:
+            A = make_workload(a)
         return A, A.num_rows, A.nnz, 0, A.num_rows, None, None
     import torch.distributed as dist
     box = [None]
     if rank == 0:
-        A = make_workload(a)
-        base = "/dev/shm" if os.path.isdir("/dev/shm") else None
-        tmp = tempfile.mkdtemp(prefix="dsp_bench_", dir=base)
-        d.save_csr(os.path.join(tmp, "A"), A)
-        del A
+        if cached:
+            tmp = key
+        elif key is not None:
+            os.makedirs(a.csr_cache, exist_ok=True)
+            generate_into(key)
+            tmp = key
+        else:
+            A = make_workload(a)
+            base = "/dev/shm" if os.path.isdir("/dev/shm") else None
+            tmp = tempfile.mkdtemp(prefix="dsp_bench_", dir=base)
+            d.save_csr(os.path.join(tmp, "A"), A)
+            del A
         box[0] = tmp
     dist.broadcast_object_list(box, src=0)
     tmp = box[0]
@@ -358,7 +400,7 @@ def load_local(a, rank, world, comm):
     comm.barrier()  # every rank has read its rows
 
     def cleanup():
-        if rank == 0:
+        if rank == 0 and key is None:
             for f in os.listdir(tmp):
                 os.unlink(os.path.join(tmp, f))
             os.rmdir(tmp)
