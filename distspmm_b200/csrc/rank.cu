@@ -371,8 +371,10 @@ int build_groups(dsp_rank *r, const dsp_csr *a, int groups) {
   return DSP_OK;
 }
 
-// Groups pipeline fetch plan: every remote row of a sparse tile is fetched with the first
-// group whose nonzeros use it, in ascending row order per (group, peer); bulk tiles with
+// Groups pipeline fetch plan: every row of a sparse tile's fetch list is fetched with the
+// first group whose nonzeros use it (rows no local nonzero uses, with the last group), in
+// ascending row order per (group, peer), so the rows moved are those of the other
+// pipelines' plan; bulk tiles with
 // local nonzeros are copied whole before group 0 (tiles without local nonzeros are
 // skipped, src/dist_spmm_node.cu:344).
 int build_group_fetch(dsp_rank *r, const dsp_rank_desc *d) {
@@ -405,12 +407,19 @@ int build_group_fetch(dsp_rank *r, const dsp_rank_desc *d) {
       first[(size_t)c] = (uint8_t)g;
     }
   }
+  // the sparse tiles' fetch lists (the rank's own needs, or the node union under the
+  // reference's scope), each row in the first group that needs it; rows that no local
+  // nonzero needs (other ranks' needs in a node list) go with the last group
   std::vector<std::vector<int32_t>> lists((size_t)G * P);
-  for (int64_t c = 0; c < r->M; ++c) {
-    const uint8_t g = first[(size_t)c];
-    if (g == 0xff) continue;
-    const int q = r->remap[(size_t)(c / r->cpt)];
-    lists[(size_t)g * P + (size_t)((q - me + P) % P)].push_back((int32_t)c);
+  for (int t = 0; t < T; ++t) {
+    const int q = r->remap[(size_t)t];
+    if (q == me || nnz_t[(size_t)t] == 0 || !r->sparse[(size_t)t]) continue;
+    const int64_t row0 = (int64_t)t * r->cpt;
+    for (int64_t p = d->needed_offsets[t]; p < d->needed_offsets[t + 1]; ++p) {
+      const int64_t c = row0 + d->needed_cols[p];
+      const int gg = first[(size_t)c] == 0xff ? G - 1 : first[(size_t)c];
+      lists[(size_t)gg * P + (size_t)((q - me + P) % P)].push_back((int32_t)c);
+    }
   }
   r->gfetch.assign((size_t)G * P, dsp_rank::Fetch());
   for (size_t i = 0; i < lists.size(); ++i) {

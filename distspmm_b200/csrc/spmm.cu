@@ -613,9 +613,13 @@ struct DiaTmaShape {
   static constexpr int kValBytes = W * kMaxDiag * 8 * 4;  // per warp: [diag][8 rows]
 };
 
+// One run of L consecutive diagonals for a warp's 8 rows: every window row the warp needs
+// and the run's values are read from shared memory first, then each lane arrives on the
+// stage's `empty` barrier (release: its reads are done, the producer may refill the stage
+// while the multiply-adds run), then the multiply-adds.
 template <int L, bool kAll>
 __device__ __forceinline__ void dia_tma_run(const float *wrow, const float *sv, int d0, const uint32_t (&pb)[4],
-                                            float4 (&acc)[8]) {
+                                            uint32_t empty_bar, float4 (&acc)[8]) {
   using V = Vec<4>;
   float v[L][8];
 #pragma unroll
@@ -625,15 +629,17 @@ __device__ __forceinline__ void dia_tma_run(const float *wrow, const float *sv, 
     v[l][0] = lo.x, v[l][1] = lo.y, v[l][2] = lo.z, v[l][3] = lo.w;
     v[l][4] = hi.x, v[l][5] = hi.y, v[l][6] = hi.z, v[l][7] = hi.w;
   }
+  float4 b[8 + L - 1];
 #pragma unroll
-  for (int k = 0; k < 8 + L - 1; ++k) {
-    const float4 b = *reinterpret_cast<const float4 *>(wrow + k * 128);
+  for (int k = 0; k < 8 + L - 1; ++k) b[k] = *reinterpret_cast<const float4 *>(wrow + k * 128);
+  mbar_arrive(empty_bar);
+#pragma unroll
+  for (int k = 0; k < 8 + L - 1; ++k)
 #pragma unroll
     for (int l = 0; l < L; ++l) {
       const int r = k - l;
-      if (r >= 0 && r < 8 && (kAll || ((pb[l] >> r) & 1u))) V::fma(acc[r], v[l][r], b);
+      if (r >= 0 && r < 8 && (kAll || ((pb[l] >> r) & 1u))) V::fma(acc[r], v[l][r], b[k]);
     }
-  }
 }
 
 template <int W, int S, int MB, bool kAccum>
@@ -651,7 +657,7 @@ __global__ void __launch_bounds__(32 * (W + 1), MB)
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(smem_addr(&full_bar[s]), 1);
-      mbar_init(smem_addr(&empty_bar[s]), W);
+      mbar_init(smem_addr(&empty_bar[s]), 32 * W);  // every consumer thread arrives
     }
     mbar_fence_init();
   }
@@ -728,27 +734,25 @@ __global__ void __launch_bounds__(32 * (W + 1), MB)
       const int s = (int)(use % S);
       if (!mbar_wait(smem_addr(&full_bar[s]), (uint32_t)((use / S) & 1), a.err, 7)) return;
       const float *wrow = win + ((size_t)s * D::kBoxRows + warp * 8) * 128 + col;
-      const uint32_t lmask = (1u << L) - 1u;
+      const uint32_t lmask = (1u << L) - 1u, eb = smem_addr(&empty_bar[s]);
       uint32_t pb[4] = {0u, 0u, 0u, 0u};
       if (((fullmask >> d0) & lmask) == lmask) {
         switch (L) {
-          case 1: dia_tma_run<1, true>(wrow, sv, d0, pb, acc); break;
-          case 2: dia_tma_run<2, true>(wrow, sv, d0, pb, acc); break;
-          case 3: dia_tma_run<3, true>(wrow, sv, d0, pb, acc); break;
-          default: dia_tma_run<4, true>(wrow, sv, d0, pb, acc); break;
+          case 1: dia_tma_run<1, true>(wrow, sv, d0, pb, eb, acc); break;
+          case 2: dia_tma_run<2, true>(wrow, sv, d0, pb, eb, acc); break;
+          case 3: dia_tma_run<3, true>(wrow, sv, d0, pb, eb, acc); break;
+          default: dia_tma_run<4, true>(wrow, sv, d0, pb, eb, acc); break;
         }
       } else {
 #pragma unroll
         for (int l = 0; l < 4; ++l) pb[l] = __shfl_sync(all, pbyte, min(d0 + l, 31));
         switch (L) {
-          case 1: dia_tma_run<1, false>(wrow, sv, d0, pb, acc); break;
-          case 2: dia_tma_run<2, false>(wrow, sv, d0, pb, acc); break;
-          case 3: dia_tma_run<3, false>(wrow, sv, d0, pb, acc); break;
-          default: dia_tma_run<4, false>(wrow, sv, d0, pb, acc); break;
+          case 1: dia_tma_run<1, false>(wrow, sv, d0, pb, eb, acc); break;
+          case 2: dia_tma_run<2, false>(wrow, sv, d0, pb, eb, acc); break;
+          case 3: dia_tma_run<3, false>(wrow, sv, d0, pb, eb, acc); break;
+          default: dia_tma_run<4, false>(wrow, sv, d0, pb, eb, acc); break;
         }
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_addr(&empty_bar[s]));
       ++use;
       d0 += L;
     }
@@ -1011,8 +1015,8 @@ EncodeTiledFn encode_tiled() {
 
 // The TMA-staged diagonal kernel for a banded launch; DSP_ERR_UNSUPPORTED (nothing launched)
 // when it does not apply: DSP_SPMM_DIA_TMA=0, no error word, or a B the tensor map cannot
-// describe. DSP_SPMM_DIA_TMA_SHAPE picks the CTA shape: 1 = two CTAs per SM of 7 consumer
-// warps with 3 stages each (the default), 2 = one CTA of 15 consumer warps with 3 stages.
+// describe. DSP_SPMM_DIA_TMA_SHAPE picks the CTA shape (consumer warps W, stages S, CTAs per
+// SM): 1 = (7, 3, 2), the default; 2 = (15, 3, 1); 3 = (6, 4, 2); 4 = (3, 5, 3).
 struct DiaTmaLaunch {
   void (*k)(const SpmmArgs, const CUtensorMap);
   int W, S, MB;
@@ -1031,8 +1035,11 @@ int launch_dia_tma(const SpmmArgs &a, bool accumulate, cudaStream_t stream) {
   EncodeTiledFn encode = encode_tiled();
   if (!encode) return DSP_ERR_UNSUPPORTED;
   const char *env_shape = getenv("DSP_SPMM_DIA_TMA_SHAPE");
-  const DiaTmaLaunch L = env_shape && atoi(env_shape) == 2 ? dia_tma_launch<15, 3, 1>(accumulate)
-                                                           : dia_tma_launch<7, 3, 2>(accumulate);
+  const int shape = env_shape ? atoi(env_shape) : 1;
+  const DiaTmaLaunch L = shape == 2   ? dia_tma_launch<15, 3, 1>(accumulate)
+                         : shape == 3 ? dia_tma_launch<6, 4, 2>(accumulate)
+                         : shape == 4 ? dia_tma_launch<3, 5, 3>(accumulate)
+                                      : dia_tma_launch<7, 3, 2>(accumulate);
   const int rows_per_item = 8 * L.W, box_rows = rows_per_item + 3;
   const size_t smem = (size_t)L.S * box_rows * 128 * sizeof(float) + (size_t)L.W * kMaxDiag * 8 * sizeof(float);
   CUtensorMap tmap;
