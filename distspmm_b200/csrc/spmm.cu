@@ -613,13 +613,11 @@ struct DiaTmaShape {
   static constexpr int kValBytes = W * kMaxDiag * 8 * 4;  // per warp: [diag][8 rows]
 };
 
-// One run of L consecutive diagonals for a warp's 8 rows: every window row the warp needs
-// and the run's values are read from shared memory first, then each lane arrives on the
-// stage's `empty` barrier (release: its reads are done, the producer may refill the stage
-// while the multiply-adds run), then the multiply-adds.
+// One run of L consecutive diagonals for a warp's 8 rows: each window row the warp needs is
+// read from shared memory once and applied to the up to L rows that use it.
 template <int L, bool kAll>
 __device__ __forceinline__ void dia_tma_run(const float *wrow, const float *sv, int d0, const uint32_t (&pb)[4],
-                                            uint32_t empty_bar, float4 (&acc)[8]) {
+                                            float4 (&acc)[8]) {
   using V = Vec<4>;
   float v[L][8];
 #pragma unroll
@@ -629,17 +627,15 @@ __device__ __forceinline__ void dia_tma_run(const float *wrow, const float *sv, 
     v[l][0] = lo.x, v[l][1] = lo.y, v[l][2] = lo.z, v[l][3] = lo.w;
     v[l][4] = hi.x, v[l][5] = hi.y, v[l][6] = hi.z, v[l][7] = hi.w;
   }
-  float4 b[8 + L - 1];
 #pragma unroll
-  for (int k = 0; k < 8 + L - 1; ++k) b[k] = *reinterpret_cast<const float4 *>(wrow + k * 128);
-  mbar_arrive(empty_bar);
-#pragma unroll
-  for (int k = 0; k < 8 + L - 1; ++k)
+  for (int k = 0; k < 8 + L - 1; ++k) {
+    const float4 b = *reinterpret_cast<const float4 *>(wrow + k * 128);
 #pragma unroll
     for (int l = 0; l < L; ++l) {
       const int r = k - l;
-      if (r >= 0 && r < 8 && (kAll || ((pb[l] >> r) & 1u))) V::fma(acc[r], v[l][r], b[k]);
+      if (r >= 0 && r < 8 && (kAll || ((pb[l] >> r) & 1u))) V::fma(acc[r], v[l][r], b);
     }
+  }
 }
 
 template <int W, int S, int MB, bool kAccum>
@@ -657,7 +653,7 @@ __global__ void __launch_bounds__(32 * (W + 1), MB)
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(smem_addr(&full_bar[s]), 1);
-      mbar_init(smem_addr(&empty_bar[s]), 32 * W);  // every consumer thread arrives
+      mbar_init(smem_addr(&empty_bar[s]), W);  // one arrival per consumer warp
     }
     mbar_fence_init();
   }
@@ -738,21 +734,23 @@ __global__ void __launch_bounds__(32 * (W + 1), MB)
       uint32_t pb[4] = {0u, 0u, 0u, 0u};
       if (((fullmask >> d0) & lmask) == lmask) {
         switch (L) {
-          case 1: dia_tma_run<1, true>(wrow, sv, d0, pb, eb, acc); break;
-          case 2: dia_tma_run<2, true>(wrow, sv, d0, pb, eb, acc); break;
-          case 3: dia_tma_run<3, true>(wrow, sv, d0, pb, eb, acc); break;
-          default: dia_tma_run<4, true>(wrow, sv, d0, pb, eb, acc); break;
+          case 1: dia_tma_run<1, true>(wrow, sv, d0, pb, acc); break;
+          case 2: dia_tma_run<2, true>(wrow, sv, d0, pb, acc); break;
+          case 3: dia_tma_run<3, true>(wrow, sv, d0, pb, acc); break;
+          default: dia_tma_run<4, true>(wrow, sv, d0, pb, acc); break;
         }
       } else {
 #pragma unroll
         for (int l = 0; l < 4; ++l) pb[l] = __shfl_sync(all, pbyte, min(d0 + l, 31));
         switch (L) {
-          case 1: dia_tma_run<1, false>(wrow, sv, d0, pb, eb, acc); break;
-          case 2: dia_tma_run<2, false>(wrow, sv, d0, pb, eb, acc); break;
-          case 3: dia_tma_run<3, false>(wrow, sv, d0, pb, eb, acc); break;
-          default: dia_tma_run<4, false>(wrow, sv, d0, pb, eb, acc); break;
+          case 1: dia_tma_run<1, false>(wrow, sv, d0, pb, acc); break;
+          case 2: dia_tma_run<2, false>(wrow, sv, d0, pb, acc); break;
+          case 3: dia_tma_run<3, false>(wrow, sv, d0, pb, acc); break;
+          default: dia_tma_run<4, false>(wrow, sv, d0, pb, acc); break;
         }
       }
+      __syncwarp();  // every lane's reads of the stage are done
+      if (lane == 0) mbar_arrive(eb);
       ++use;
       d0 += L;
     }

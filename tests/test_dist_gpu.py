@@ -209,9 +209,9 @@ def test_group_split_pipeline_widths(gpu, rmat12, dims):
 
 
 def _auto_pipeline(g, p, A):
-    """The AUTO rule restated: split when whole rows would leave most nonzeros behind the
-    fetches (rows-pipeline phase 0 < 1/2), the owned tiles hold >= 30 % of them and the
-    pieces accumulated after a row's first phase average >= 12 nonzeros."""
+    """The AUTO rule restated: whole rows (1) when the rows needing only owned tiles hold at
+    least half the nonzeros; else split (2) when the owned tiles hold >= 30 % of them and the
+    pieces accumulated after a row's first phase average >= 12 nonzeros; else row groups (3)."""
     lb, ub = g.bounds[p]
     ip = np.asarray(A.indptr[lb:ub + 1]) - A.indptr[lb]
     cols = np.asarray(A.indices[A.indptr[lb]:A.indptr[ub]])
@@ -226,7 +226,9 @@ def _auto_pipeline(g, p, A):
     np.minimum.at(first, rowid, pos)
     acc_nnz = int((pos != first[rowid]).sum())
     acc_pieces = np.unique(rowid.astype(np.int64) * len(g.ranks) + pos).size - int((np.diff(ip) > 0).sum())
-    return 2 if (2 * phase0 < nnz and 10 * local >= 3 * nnz and acc_pieces > 0 and acc_nnz >= 12 * acc_pieces) else 1
+    if 2 * phase0 >= nnz:
+        return 1
+    return 2 if (10 * local >= 3 * nnz and acc_pieces > 0 and acc_nnz >= 12 * acc_pieces) else 3
 
 
 def test_pipeline_auto_choice(gpu, rmat12):
