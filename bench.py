@@ -714,13 +714,15 @@ def main(argv=None):
     fetch_bytes = st["fetch_bytes"]
     # per rank: nonzeros, rows, phase structure, SpMM time, time waiting for fetches, bytes
     mine = [st["nnz_local"], st["m_local"], st["pipeline"], int(mean_compute * 1e4), int(idle * 1e4),
-            st["fetch_bytes"] // 1024]
+            st["fetch_bytes"] // 1024, int(st["model_rows_ms"] * 1e4), int(st["model_split_ms"] * 1e4),
+            int(st["model_groups_ms"] * 1e4)]
     per_rank = [mine]
     if comm is not None:
         fetch_bytes = comm.allreduce_sum_i64(fetch_bytes)
         per_rank = [[int(x) for x in r] for r in comm.allgather_i32(np.array(mine, np.int64).clip(max=2**31 - 1))]
     ranks = [{"nnz": r[0], "rows": r[1], "pipeline": ["", "rows", "split", "groups"][r[2]], "compute_ms": r[3] / 1e4,
-              "idle_ms": r[4] / 1e4, "fetched_kib": r[5]} for r in per_rank]
+              "idle_ms": r[4] / 1e4, "fetched_kib": r[5],
+              "auto_model_ms": {"rows": r[6] / 1e4, "split": r[7] / 1e4, "groups": r[8] / 1e4}} for r in per_rank]
     traffic = profile_traffic(workload_name(a)) if world == 1 else None
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": a.steps,

@@ -62,7 +62,8 @@ class dsp_rank_stats(ctypes.Structure):
     _fields_ = [(n, c_i64) for n in ("m_local", "nnz_local", "segments", "fetch_rows", "fetch_bytes",
                                      "fetch_bulk_tiles", "fetch_sparse_tiles", "owned_rows",
                                      "distinct_cols", "launches_per_step", "kernels_per_step",
-                                     "device_bytes", "pipeline", "phase0_nnz", "timeline_len")]
+                                     "device_bytes", "pipeline", "phase0_nnz", "timeline_len")] + [
+        (n, ctypes.c_float) for n in ("model_rows_ms", "model_split_ms", "model_groups_ms")]
 
 
 class dsp_args(ctypes.Structure):

@@ -63,8 +63,9 @@ using namespace dsp;
 
 struct dsp_rank {
   int me = 0, P = 1, device = 0, dims = 0, T = 0, n_streams = 1, fetch_engine = DSP_FETCH_LSU;
-  int *d_err = nullptr;  // set by a fetch kernel whose bounded wait gave up
+  int *d_err = nullptr;  // set by a fetch or SpMM kernel whose bounded wait gave up
   int64_t cpt = 0, M = 0, m_lb = 0, m_local = 0, nnz_local = 0;
+  float model_ms[3] = {0.f, 0.f, 0.f};  // modelled step of the rows / split / groups pipelines
   std::vector<int32_t> remap;
   std::vector<uint8_t> sparse;
   float *B = nullptr, *C = nullptr, *scratch = nullptr;
@@ -161,7 +162,43 @@ int build_split_phases(dsp_rank *r, const dsp_csr *a, const std::vector<int32_t>
 // would run before any fetch lands) cuts rows by ring position instead.
 int build_groups(dsp_rank *r, const dsp_csr *a, int groups);
 
-int build_phases(dsp_rank *r, const dsp_csr *a, int pipeline, int groups) {
+// Rows this rank's fetch moves per step (what build_fetch / build_group_fetch will list):
+// whole bulk tiles and the sparse tiles' lists, for remote tiles holding local nonzeros.
+int64_t planned_fetch_rows(const dsp_rank *r, const dsp_rank_desc *d) {
+  if (r->P == 1) return 0;
+  std::vector<int64_t> nnz_t((size_t)r->T, 0);
+  for (int64_t j = 0; j < d->local->nnz; ++j) nnz_t[(size_t)(d->local->indices[j] / r->cpt)]++;
+  int64_t rows = 0;
+  for (int t = 0; t < r->T; ++t) {
+    if (r->remap[(size_t)t] == r->me || nnz_t[(size_t)t] == 0) continue;
+    rows += r->sparse[(size_t)t] ? d->needed_offsets[t + 1] - d->needed_offsets[t]
+                                 : std::min<int64_t>(r->cpt, r->M - (int64_t)t * r->cpt);
+  }
+  return rows;
+}
+
+// Step-time model of the three phase structures for DSP_PIPELINE_AUTO, in seconds. One
+// nonzero costs a B-row gather (dims x 4 bytes at ~10 TB/s through L2); one fetched row
+// dims x 4 bytes over NVLink at ~730 GB/s; an accumulated piece a C-row read and write (two
+// gathers' worth); every extra segment of the groups pipeline ~60 us (the partial last wave
+// of its launch). Fitted to R-MAT 24 on 2 x B200 (per rank: split 13.95 / groups 14.42 /
+// rows 16.00 ms on the hub rank, rows 14.30 / split 14.67 / groups 15.54 on the other).
+struct PipelineModel {
+  double rows, split, groups;
+};
+
+PipelineModel pipeline_model(int dims, int64_t nnz, int64_t phase0_nnz, int64_t local_nnz, int64_t split_pieces,
+                             int64_t group_pieces, int64_t fetch_rows, int G) {
+  const double t_nnz = dims * 4.0 / 10e12, t_fetch = fetch_rows * (dims * 4.0) / 730e9;
+  const double all = nnz * t_nnz, p0 = phase0_nnz * t_nnz, loc = local_nnz * t_nnz;
+  PipelineModel m;
+  m.rows = std::max(t_fetch, p0) + (all - p0);
+  m.split = std::max(t_fetch, loc) + (all - loc) + 2.0 * split_pieces * t_nnz;
+  m.groups = std::max(t_fetch + (all - loc) / std::max(G, 1), all) + 2.0 * group_pieces * t_nnz + G * 60e-6;
+  return m;
+}
+
+int build_phases(dsp_rank *r, const dsp_csr *a, int pipeline, int groups, int64_t fetch_rows) {
   const int P = r->P, me = r->me;
   const int64_t m = a->num_rows, cpt = r->cpt;
   std::vector<int32_t> phase((size_t)std::max<int64_t>(m, 1), -1), first((size_t)std::max<int64_t>(m, 1), -1);
@@ -193,29 +230,34 @@ int build_phases(dsp_rank *r, const dsp_csr *a, int pipeline, int groups) {
     if (rc) return rc;
   }
   r->segs.resize((size_t)P);
-  // nonzeros in tiles this rank owns: what the split pipeline computes before any fetch
-  // split pipeline shape: pieces (row, phase) beyond each row's first one are accumulated
-  // into C (a read-modify-write of the row), with acc_nnz nonzeros among them
-  int64_t local_nnz = 0, acc_pieces = 0, acc_nnz = 0;
+  // local_nnz: nonzeros in tiles this rank owns (what split and groups compute before any
+  // fetch); acc_pieces: pieces (row, ring position) after each row's first one, which the split
+  // pipeline accumulates into C; group_pieces: rows with both owned and remote nonzeros,
+  // which the groups pipeline accumulates once
+  int64_t local_nnz = 0, acc_pieces = 0, group_pieces = 0;
   for (int64_t i = 0; i < m; ++i) {
     if (touched[(size_t)i] > 1) acc_pieces += touched[(size_t)i] - 1;
-    for (int64_t j = a->indptr[i]; j < a->indptr[i + 1]; ++j) {
-      const int32_t k = (r->remap[(size_t)(a->indices[j] / cpt)] - me + P) % P;
-      local_nnz += k == 0;
-      acc_nnz += k != first[(size_t)i];
+    if (touched[(size_t)i] > 1 && first[(size_t)i] == 0) group_pieces++;
+    for (int64_t j = a->indptr[i]; j < a->indptr[i + 1]; ++j)
+      local_nnz += (r->remap[(size_t)(a->indices[j] / cpt)] - me + P) % P == 0;
+  }
+  // AUTO: whole rows when the rows needing only owned tiles hold at least half the
+  // nonzeros (they hide the fetch: stencils); otherwise the structure with the shortest
+  // modelled step, whole rows kept unless another is >= 3 % shorter (the model leaves out
+  // the fetch kernels' share of the SMs, which weighs on the overlapped forms).
+  const int G = (int)std::max<int64_t>(1, std::min<int64_t>({groups > 0 ? groups : 8, std::max<int64_t>(m, 1), 253}));
+  const PipelineModel model =
+      pipeline_model(r->dims, a->nnz, rows_phase0_nnz, local_nnz, acc_pieces, group_pieces, fetch_rows, G);
+  r->model_ms[0] = (float)(model.rows * 1e3);
+  r->model_ms[1] = (float)(model.split * 1e3);
+  r->model_ms[2] = (float)(model.groups * 1e3);
+  if (pipeline == DSP_PIPELINE_AUTO) {
+    pipeline = DSP_PIPELINE_ROWS;
+    if (2 * rows_phase0_nnz < a->nnz) {
+      const double best = std::min(model.split, model.groups);
+      if (best < 0.97 * model.rows) pipeline = model.split <= model.groups ? DSP_PIPELINE_SPLIT : DSP_PIPELINE_GROUPS;
     }
   }
-  // AUTO: split only when whole rows would leave most of the work behind the fetches, the
-  // owned tiles hold enough work (>= 30 %) to hide them, and the accumulated pieces are long
-  // (>= 12 nonzeros each). Measured on B200: uniform 32/row at P = 2 (50 % local, 16 per
-  // accumulated piece) +10 % split; R-MAT at P = 2 (the hub rank 16 % local; the other 86 %
-  // local but 8.7 per accumulated piece) and P = 4 (8.4) slower split; the stencil is
-  // rows-bound.
-  if (pipeline == DSP_PIPELINE_AUTO)
-    pipeline = 2 * rows_phase0_nnz >= a->nnz ? DSP_PIPELINE_ROWS
-               : 10 * local_nnz >= 3 * a->nnz && acc_pieces > 0 && acc_nnz >= 12 * acc_pieces
-                   ? DSP_PIPELINE_SPLIT
-                   : DSP_PIPELINE_GROUPS;
   if (P == 1 || P > 64) pipeline = DSP_PIPELINE_ROWS;
   r->pipeline = pipeline;
   if (pipeline == DSP_PIPELINE_GROUPS) return build_groups(r, a, groups);
@@ -489,7 +531,7 @@ extern "C" int dsp_rank_create(const dsp_rank_desc *d, dsp_rank **out) {
     return bail(fail(DSP_ERR_NOMEM, "C (%zu bytes): %s", cbytes, cudaGetErrorString(e)));
   if ((e = cudaMalloc(&r->d_err, sizeof(int))) != cudaSuccess || (e = cudaMemset(r->d_err, 0, sizeof(int))) != cudaSuccess)
     return bail(fail(DSP_ERR_NOMEM, "error flag: %s", cudaGetErrorString(e)));
-  if ((rc = build_phases(r, d->local, d->pipeline, d->groups))) return bail(rc);
+  if ((rc = build_phases(r, d->local, d->pipeline, d->groups, planned_fetch_rows(r, d)))) return bail(rc);
   if (r->P > 1 && (rc = r->n_groups > 0 ? build_group_fetch(r, d) : build_fetch(r, d))) return bail(rc);
   if (r->scratch_floats > 0 && (e = cudaMalloc(&r->scratch, sizeof(float) * (size_t)r->scratch_floats)) != cudaSuccess)
     return bail(fail(DSP_ERR_NOMEM, "scratch: %s", cudaGetErrorString(e)));
@@ -540,6 +582,9 @@ extern "C" int dsp_rank_create(const dsp_rank_desc *d, dsp_rank **out) {
   }
   for (auto &F : r->gfetch) s.kernels_per_step += F.n_rows > 0;
   s.timeline_len = std::max(r->P, n_seg);
+  s.model_rows_ms = r->model_ms[0];
+  s.model_split_ms = r->model_ms[1];
+  s.model_groups_ms = r->model_ms[2];
   s.launches_per_step += s.kernels_per_step;
   for (int64_t t : r->owned) s.owned_rows += std::max<int64_t>(0, std::min<int64_t>(r->cpt, r->M - t * r->cpt));
   {

@@ -172,7 +172,8 @@ class Rank:
     def stats(self) -> dict:
         s = dsp_rank_stats()
         call("dsp_rank_stats_get", self._h, ctypes.byref(s))
-        return {k: int(getattr(s, k)) for k, _ in dsp_rank_stats._fields_}
+        return {k: (round(float(getattr(s, k)), 4) if t is ctypes.c_float else int(getattr(s, k)))
+                for k, t in dsp_rank_stats._fields_}
 
     def close(self) -> None:
         if getattr(self, "_h", None):

@@ -370,6 +370,8 @@ typedef struct dsp_rank_stats {
   int64_t pipeline;          /* DSP_PIPELINE_ROWS, _SPLIT or _GROUPS in use      */
   int64_t phase0_nnz;        /* nonzeros computed before any fetch lands         */
   int64_t timeline_len;      /* entries of dsp_rank_last_timeline (max(P, groups)) */
+  /* DSP_PIPELINE_AUTO's step-time model of the three phase structures for this rank (ms) */
+  float model_rows_ms, model_split_ms, model_groups_ms;
 } dsp_rank_stats;
 
 int dsp_rank_create(const dsp_rank_desc *d, dsp_rank **out);

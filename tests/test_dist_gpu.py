@@ -208,27 +208,42 @@ def test_group_split_pipeline_widths(gpu, rmat12, dims):
     g.close()
 
 
-def _auto_pipeline(g, p, A):
+def _auto_pipeline(g, p, A, dims):
     """The AUTO rule restated: whole rows (1) when the rows needing only owned tiles hold at
-    least half the nonzeros; else split (2) when the owned tiles hold >= 30 % of them and the
-    pieces accumulated after a row's first phase average >= 12 nonzeros; else row groups (3)."""
+    least half the nonzeros; otherwise the modelled step time of rows (1), split (2) and row
+    groups (3) per rank — a nonzero one B-row gather at 10 TB/s, a fetched row over NVLink at
+    730 GB/s, an accumulated piece two gathers, a group segment 60 us — with rows kept
+    unless the best other is >= 3 % shorter."""
     lb, ub = g.bounds[p]
     ip = np.asarray(A.indptr[lb:ub + 1]) - A.indptr[lb]
     cols = np.asarray(A.indices[A.indptr[lb]:A.indptr[ub]])
-    pos = (g.plan.remap[cols // g.plan.cpt] - p) % len(g.ranks)
-    rowid = np.repeat(np.arange(ub - lb), np.diff(ip))
-    last = np.full(ub - lb, -1)
+    P = len(g.ranks)
+    pos = (g.plan.remap[cols // g.plan.cpt] - p) % P
+    m = ub - lb
+    rowid = np.repeat(np.arange(m), np.diff(ip))
+    last = np.full(m, -1)
     np.maximum.at(last, rowid, pos)
     phase0 = int(np.diff(ip)[last == 0].sum())
     local = int((pos == 0).sum())
     nnz = int(ip[-1])
-    first = np.full(ub - lb, len(g.ranks))
-    np.minimum.at(first, rowid, pos)
-    acc_nnz = int((pos != first[rowid]).sum())
-    acc_pieces = np.unique(rowid.astype(np.int64) * len(g.ranks) + pos).size - int((np.diff(ip) > 0).sum())
     if 2 * phase0 >= nnz:
         return 1
-    return 2 if (10 * local >= 3 * nnz and acc_pieces > 0 and acc_nnz >= 12 * acc_pieces) else 3
+    first = np.full(m, P)
+    np.minimum.at(first, rowid, pos)
+    touched = np.zeros(m, np.int64)
+    np.add.at(touched, np.unique(rowid.astype(np.int64) * P + pos) // P, 1)
+    acc_pieces = int(np.maximum(touched - 1, 0).sum())
+    group_pieces = int(((touched > 1) & (first == 0)).sum())
+    fetch_rows = g.ranks[p].stats()["fetch_rows"]
+    G = max(1, min(8, max(m, 1), 253))
+    t_nnz, t_fetch = dims * 4.0 / 10e12, fetch_rows * dims * 4.0 / 730e9
+    t_all, t_p0, t_loc = nnz * t_nnz, phase0 * t_nnz, local * t_nnz
+    rows = max(t_fetch, t_p0) + (t_all - t_p0)
+    split = max(t_fetch, t_loc) + (t_all - t_loc) + 2.0 * acc_pieces * t_nnz
+    groups = max(t_fetch + (t_all - t_loc) / G, t_all) + 2.0 * group_pieces * t_nnz + G * 60e-6
+    if min(split, groups) < 0.97 * rows:
+        return 2 if split <= groups else 3
+    return 1
 
 
 def test_pipeline_auto_choice(gpu, rmat12):
@@ -237,7 +252,7 @@ def test_pipeline_auto_choice(gpu, rmat12):
     needing the peer)."""
     from distspmm_b200.dist import build_local_group
     g = build_local_group(rmat12, 4, _devices(4), 64, 4, 2, 2, partition="balanced", fetch_scope="rank")
-    assert [r.stats()["pipeline"] for r in g.ranks] == [_auto_pipeline(g, p, rmat12) for p in range(4)]
+    assert [r.stats()["pipeline"] for r in g.ranks] == [_auto_pipeline(g, p, rmat12, 64) for p in range(4)]
     g.close()
     U = d.gen_uniform(4096, 32, seed=3)
     g = build_local_group(U, 2, _devices(2), 64, 4, 2, 2, partition="balanced", fetch_scope="rank")
