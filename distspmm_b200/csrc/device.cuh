@@ -60,6 +60,7 @@ struct SpmmArgs {
   int n_runs;                    // runs of consecutive offsets (o, o+1, ..., at most 4 long)
   uint8_t run_len[kMaxDiag];     // in offset order
   int *err;  // device error word set by a kernel whose bounded wait gave up (nullptr: none)
+  uint32_t wait_hint_ns;  // suspend-time hint of the staged kernels' mbarrier waits (0: none)
 };
 
 struct SpmmShape {

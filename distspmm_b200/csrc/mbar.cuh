@@ -51,4 +51,26 @@ __device__ __forceinline__ bool mbar_wait(uint32_t mbar, uint32_t parity, int *e
   }
 }
 
+// As mbar_wait, with a suspend-time hint: a thread whose phase is not complete may sleep up
+// to hint_ns nanoseconds inside try_wait (woken when the phase completes) instead of
+// returning at once, so waiting warps leave the issue slots to working ones.
+__device__ __forceinline__ bool mbar_wait_hint(uint32_t mbar, uint32_t parity, uint32_t hint_ns, int *err, int code,
+                                               long long budget = kMbarWaitCycles) {
+  if (hint_ns == 0) return mbar_wait(mbar, parity, err, code, budget);
+  const long long t0 = clock64();
+  while (true) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(done)
+        : "r"(mbar), "r"(parity), "r"(hint_ns)
+        : "memory");
+    if (done) return true;
+    if (clock64() - t0 > budget) {
+      if (err) atomicExch(err, code);
+      return false;
+    }
+  }
+}
+
 }  // namespace dsp

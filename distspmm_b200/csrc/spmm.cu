@@ -671,7 +671,7 @@ __global__ void __launch_bounds__(32 * (W + 1), MB)
       for (int q = 0; q < a.n_runs; ++q) {
         const int s = (int)(use % S);
         const int64_t j = use / S;
-        if (j > 0 && !mbar_wait(smem_addr(&empty_bar[s]), (uint32_t)((j - 1) & 1), a.err, 5)) {
+        if (j > 0 && !mbar_wait_hint(smem_addr(&empty_bar[s]), (uint32_t)((j - 1) & 1), a.wait_hint_ns, a.err, 5)) {
           ok = false;
           break;
         }
@@ -728,7 +728,7 @@ __global__ void __launch_bounds__(32 * (W + 1), MB)
     for (int q = 0; q < a.n_runs; ++q) {
       const int L = a.run_len[q];
       const int s = (int)(use % S);
-      if (!mbar_wait(smem_addr(&full_bar[s]), (uint32_t)((use / S) & 1), a.err, 7)) return;
+      if (!mbar_wait_hint(smem_addr(&full_bar[s]), (uint32_t)((use / S) & 1), a.wait_hint_ns, a.err, 7)) return;
       const float *wrow = win + ((size_t)s * D::kBoxRows + warp * 8) * 128 + col;
       const uint32_t lmask = (1u << L) - 1u, eb = smem_addr(&empty_bar[s]);
       uint32_t pb[4] = {0u, 0u, 0u, 0u};
@@ -1062,7 +1062,10 @@ int launch_dia_tma(const SpmmArgs &a, bool accumulate, cudaStream_t stream) {
   }
   const int64_t items = (a.dia_m + rows_per_item - 1) / rows_per_item * (a.N / 128);
   const int64_t grid = std::min<int64_t>(items, (int64_t)std::max(sms, 1) * L.MB);
-  L.k<<<(unsigned)grid, 32 * (L.W + 1), smem, stream>>>(a, tmap);
+  SpmmArgs la = a;
+  const char *env_hint = getenv("DSP_SPMM_WAIT_HINT_NS");  // suspend-time hint of the waits
+  la.wait_hint_ns = env_hint ? (uint32_t)std::max(0, std::min(atoi(env_hint), 1000000)) : 0u;
+  L.k<<<(unsigned)grid, 32 * (L.W + 1), smem, stream>>>(la, tmap);
   return DSP_OK;
 }
 

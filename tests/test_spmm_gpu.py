@@ -225,6 +225,7 @@ DIA_KERNELS = {
     "tma_15": {"DSP_SPMM_DIA_TMA": "1", "DSP_SPMM_DIA_TMA_SHAPE": "2"},
     "tma_6x2": {"DSP_SPMM_DIA_TMA": "1", "DSP_SPMM_DIA_TMA_SHAPE": "3"},
     "tma_3x3": {"DSP_SPMM_DIA_TMA": "1", "DSP_SPMM_DIA_TMA_SHAPE": "4"},
+    "tma_7x2_wait_hint": {"DSP_SPMM_DIA_TMA": "1", "DSP_SPMM_DIA_TMA_SHAPE": "1", "DSP_SPMM_WAIT_HINT_NS": "2000"},
     "reg_8": {"DSP_SPMM_DIA_TMA": "0", "DSP_SPMM_DIA_ROWS": "8"},
     "reg_4": {"DSP_SPMM_DIA_TMA": "0", "DSP_SPMM_DIA_ROWS": "4"},
 }
@@ -298,7 +299,7 @@ def test_stencil_diagonal_kernel_widths(gpu, monkeypatch, kernel):
         plan.check_error()
 
 
-@pytest.mark.parametrize("kernel", ["tma_7x2", "tma_15", "tma_6x2", "tma_3x3"])
+@pytest.mark.parametrize("kernel", ["tma_7x2", "tma_15", "tma_6x2", "tma_3x3", "tma_7x2_wait_hint"])
 def test_banded_tma_windows_many_items_per_cta(gpu, monkeypatch, kernel):
     """Enough rows that every persistent CTA of the TMA-staged kernel takes many items, so
     its stage ring wraps many times (bounded waits on both barriers of every stage); holes
