@@ -441,6 +441,11 @@ __global__ void __launch_bounds__(kSpmmThreads, kMinBlocks) spmm_warp_kernel(con
     for (int w = 0; w < VPL; ++w) V::fma(acc[w], v, b[w]);
   };
 
+  // B rows as float4 from this lane's first column: one 32 x 32 -> 64-bit multiply-add per
+  // nonzero (the host keeps ldb / 4 within int32 for this kernel)
+  const float4 *B4 = reinterpret_cast<const float4 *>(a.B + col0);
+  const int32_t ld4 = (int32_t)(a.ldb >> 2);
+
   // full steps of U nonzeros: p stays a multiple of 4 (chunk_nnz is a multiple of 16), so
   // the column ids, values and row ids of 4 nonzeros come in one 16-byte load each, and no
   // entry needs a bounds test
@@ -460,19 +465,31 @@ __global__ void __launch_bounds__(kSpmmThreads, kMinBlocks) spmm_warp_kernel(con
     float4 b[U][VPL];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const float *brow = a.B + (int64_t)col_id(cs[u]) * a.ldb + col0;
+      const float4 *brow = B4 + (int64_t)col_id(cs[u]) * ld4;
       const uint64_t pol = col_policy(cs[u], pol_hot, pol_cold);
 #pragma unroll
-      for (int w = 0; w < VPL; ++w) b[u][w] = V::ldg(brow + 128 * w, pol);
+      for (int w = 0; w < VPL; ++w) b[u][w] = V::ldg(reinterpret_cast<const float *>(brow + 32 * w), pol);
     }
+    // the step stays in the current row (the common case on rows longer than a step): the
+    // multiply-adds without per-nonzero row tests
+    bool same = true;
 #pragma unroll
-    for (int u = 0; u < U; ++u) add(r[u], v[u], b[u]);
+    for (int u = 0; u < U; ++u) same &= r[u] == row;
+    if (same) {
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+#pragma unroll
+        for (int w = 0; w < VPL; ++w) V::fma(acc[w], v[u], b[u][w]);
+    } else {
+#pragma unroll
+      for (int u = 0; u < U; ++u) add(r[u], v[u], b[u]);
+    }
   }
   // the chunk's last nonzeros (the matrix's end)
   for (; p < e; ++p) {
     const int32_t cs = __ldg(a.cols + p);
     float4 b[VPL];
-    const float *brow = a.B + (int64_t)col_id(cs) * a.ldb + col0;
+    const float *brow = reinterpret_cast<const float *>(B4 + (int64_t)col_id(cs) * ld4);
 #pragma unroll
     for (int w = 0; w < VPL; ++w) b[w] = V::ldg(brow + 128 * w, col_policy(cs, pol_hot, pol_cold));
     add(__ldg(a.coo_row + p), __ldg(a.vals + p), b);
@@ -909,7 +926,8 @@ WarpShape warp_shape(int N, const float *B, int64_t ldb, const float *C, int64_t
     return e ? atoi(e) : 0;
   }();
   WarpShape w;
-  if (!env_on || N <= 0 || N % 128 != 0 || ldb % 4 != 0 || ldc % 4 != 0 || !aligned(B, 16) || !aligned(C, 16))
+  if (!env_on || N <= 0 || N % 128 != 0 || ldb % 4 != 0 || ldb / 4 > INT32_MAX || ldc % 4 != 0 || !aligned(B, 16) ||
+      !aligned(C, 16))
     return w;
   // 4 nonzeros per step. N = 128: one float4 per lane, registers held to 48 so that 5 blocks
   // (40 warps) fit an SM (R-MAT scale 20: 1.32 ms against 1.46 uncapped and 1.92 with 8
