@@ -577,9 +577,11 @@ def main(argv=None):
     else:
         n_dev, worst_dev = 0, 0.0
 
-    # compute-stream time spent waiting for fetches in the last step (segments not back to back)
+    # compute-stream time spent waiting for fetches in the last step: from the step's start
+    # (timeline origin) to the last segment's end, minus the segments' own durations, so a
+    # wait before the first segment (an empty owned phase) counts too
     segs = [(t[2], t[3]) for t in timeline if t[2] is not None]
-    idle = (segs[-1][1] - segs[0][0]) - sum(e - b for b, e in segs) if segs else 0.0
+    idle = max(0.0, segs[-1][1] - sum(e - b for b, e in segs)) if segs else 0.0
     idle_max = comm.allreduce_max(idle) if comm is not None else idle
     mean_step = statistics.mean(step_ms)
     mean_compute = statistics.mean(compute_ms)
