@@ -502,11 +502,13 @@ def main(argv=None):
 
     t_setup = time.perf_counter()
     local, M, nnz, lb, ub, cleanup, rows_for = load_local(a, rank, world, comm)
+    t_loaded = time.perf_counter()
     if comm is None:
         tiling = planner.tile(local, a.n_rolls)
         plan = global_plan([tiling], a.task_dist, a.n_rolls)
     else:
         tiling, plan = distributed_plan(comm, local, a.n_rolls, a.task_dist)
+    t_planned = time.perf_counter()
 
     def new_rank():
         X = make_rank(local, rank, world, local_rank, a.dims, M, lb, tiling, plan, a.comm_type, a.platform,
@@ -523,6 +525,10 @@ def main(argv=None):
     if comm is not None:
         comm.barrier()
     setup_s = time.perf_counter() - t_setup
+    # where set-up goes: matrix generation / reading, tiling + allocation + lists, the
+    # rank's device operands and fetch plan (with B filled)
+    setup_parts = {"load_s": round(t_loaded - t_setup, 1), "plan_s": round(t_planned - t_loaded, 1),
+                   "rank_s": round(setup_s - (t_planned - t_setup), 1)}
     flush = torch.empty(512 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
 
     def flush_l2():
@@ -742,7 +748,7 @@ def main(argv=None):
                    "max_rank_compute_ms": round(t_comp_max, 4),
                    "max_rank_compute_idle_ms": round(idle_max, 4),
                    "timeline_rank0": timeline if rank == 0 else None, "ranks": ranks},
-        "wall_s_timed_region": round(wall, 3), "setup_s": round(setup_s, 1),
+        "wall_s_timed_region": round(wall, 3), "setup_s": round(setup_s, 1), "setup_parts": setup_parts,
         "gather": gather,
     }
     R.close()
